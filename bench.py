@@ -1,0 +1,454 @@
+"""Benchmark of the B200 contraction hot path (one JSON line on rank 0).
+
+Headline workload: dense permutedims of a rank-6 16^6 tensor (16,777,216
+elements) in f64 with perm (5,3,1,0,4,2), entries N(0,1) from a seed.  A
+step permutes one batch of `--batch` such tensors (distinct buffers, so every
+input comes from HBM: each tensor is 134 MB and the batch is ~4.3 GB, far
+larger than the 126 MB L2).  Metric unit: GB/s of algorithmic traffic,
+2 * 16^6 * 8 bytes per tensor.  With --gpus N the permute runs as N
+independent replicas (one process per GPU, no collective on the data path);
+`value` is the sum over ranks.
+
+Also reported on the same line (`contraction`): the dense f64 MPS two-site
+merge A[256,4,256] x B[256,4,256] -> C[256,4,4,256] (FP64 tensor-core
+TFLOP/s), and the complex128 permute of the same 16^6 shape.
+
+--impl reference times the reference's CPU algorithm for the same workload
+on the host cores (the C restatement of GenericBackend::permute_into,
+backend/generic.rs:15-39, spread over all host threads).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "ndtensors-rs_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "f64 contraction TFLOP/s and permutedims GB/s at 1/2/4/8 B200 vs host CPU"
+SHAPE = (16,) * 6
+PERM = (5, 3, 1, 0, 4, 2)
+NELEM = 16**6
+BYTES_F64 = 2 * NELEM * 8  # algorithmic bytes per tensor (read + write)
+FP64_DMMA_PEAK_TFLOPS = 37.1  # measured mma.sync f64 microbenchmark on this pool's B200 (profiles/fp64_peak.txt)
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------ helpers
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+def ncu_traffic(key):
+    """Per-launch DRAM bytes (read + write) recorded from an ncu capture."""
+    p = ROOT / "profiles" / "ncu_traffic.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == key:
+            try:
+                return float(parts[1])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during the timed
+    region (the same data nvidia-smi's clocks query reports)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index):
+        self.samples, self.reasons = [], set()
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # no NVML: report nothing rather than guess
+            log("clock sampling unavailable:", e)
+        self._stop = threading.Event()
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def result(self):
+        if not self.ok or not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+# ------------------------------------------------------------ CPU baseline
+def cpu_permute_time(threads, sample_tensors=1, seed=2002):
+    """Times the oracle's restatement of GenericBackend::permute_into over
+    the full 16^6 f64 tensor, `threads` host threads splitting the source
+    index range (ctypes releases the GIL)."""
+    import numpy as np
+
+    from oracle import oracle as o
+
+    L = o.lib()
+    rng = np.random.default_rng(seed)
+    a = np.ascontiguousarray(rng.standard_normal(NELEM))
+    dst = np.zeros(NELEM)
+    shape = o._sz(SHAPE)
+    perm = o._sz(PERM)
+    chunks = [(NELEM * i // threads, NELEM * (i + 1) // threads) for i in range(threads)]
+
+    def work(lo, hi):
+        L.ndo_permutedims_range(0, a.ctypes.data_as(ctypes.c_void_p), shape, ctypes.c_size_t(6), perm,
+                                dst.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(lo), ctypes.c_size_t(hi))
+
+    t0 = time.perf_counter()
+    for _ in range(sample_tensors):
+        ts = [threading.Thread(target=work, args=c) for c in chunks]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+    dt = time.perf_counter() - t0
+    return dt / sample_tensors
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return  # rank 0 alone runs the host-CPU reference
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        cpu_permute_time(threads)
+    times = [cpu_permute_time(threads) for _ in range(args.steps)]
+    t = sum(times)
+    value = BYTES_F64 * args.steps / t / 1e9
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / args.steps,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f64",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "permutedims 16^6 f64 perm (5,3,1,0,4,2)", "batch": 1,
+                   "l2": "input 134 MB > 126 MB L2"},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"full 16^6 f64 tensor per step, {threads} host threads over the source index range"},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- ours
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--no-extras", action="store_true", help="skip the contraction sub-results")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args)
+
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import numpy as np
+    import torch
+
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+
+    import ndtensors_b200 as ndt
+
+    lib = ndt.get_lib()
+    stream = torch.cuda.current_stream()
+    ndt.set_stream(stream.cuda_stream)
+
+    # ---- inputs resident in HBM: `batch` distinct tensors (seeded)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1002 + rank)
+    B = args.batch
+    src = torch.randn(B, NELEM, dtype=torch.float64, device="cuda", generator=g)
+    dst = torch.empty_like(src)
+    shape_c = (ctypes.c_size_t * 6)(*SHAPE)
+    perm_c = (ctypes.c_size_t * 6)(*PERM)
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+
+    def step():
+        for i in range(B):
+            st = lib.ndt_b200_permutedims_dev(0, ctypes.c_void_p(src[i].data_ptr()), ctypes.c_void_p(dst[i].data_ptr()),
+                                              shape_c, 6, perm_c, 6, sptr)
+            if st != 0:
+                raise RuntimeError(f"permutedims failed: {st} {ndt.last_error()}")
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # parity spot check of the timed kernel on a slice (bit-exact vs torch permute)
+    ref0 = src[0].view(*reversed(SHAPE)).permute(*[5 - p for p in reversed(PERM)]).contiguous()
+    assert torch.equal(ref0.flatten(), dst[0]), "permute mismatch"
+
+    # per-launch durations of the dominant kernel inside the timed region
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    launches0 = ndt.launch_count()
+    sampler = ClockSampler(torch.cuda.current_device())
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with sampler:
+        t0.record()
+        for k in range(args.steps):
+            ev[k][0].record()
+            step()
+            ev[k][1].record()
+        t1.record()
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    launches = ndt.launch_count() - launches0
+    ms = t0.elapsed_time(t1)
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    ms_t = torch.tensor([ms], device="cuda")
+    if pg:
+        pg.all_reduce(ms_t, op=pg.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+    total_bytes = BYTES_F64 * B * args.steps * world
+    value = total_bytes / (ms_max * 1e-3) / 1e9
+    launch_ms = statistics.mean(step_ms) / B
+    achieved = BYTES_F64 / (launch_ms * 1e-3) / 1e9
+    peaks, peak_src = measured_peaks()
+
+    # ---- end to end through the C ABI with host buffers (pinned)
+    e2e = None
+    host_in = torch.empty(NELEM, dtype=torch.float64, pin_memory=True)
+    host_in.copy_(src[0].cpu())
+    hp = ctypes.cast(host_in.data_ptr(), ctypes.POINTER(ctypes.c_double))
+    st = ctypes.c_int(-999)
+
+    def e2e_step():
+        t = lib.ndt_tensor_f64_from_data(hp, NELEM, shape_c, 6, ctypes.byref(st))
+        p = lib.ndt_tensor_f64_permutedims(t, perm_c, 6, ctypes.byref(st))
+        d = lib.ndt_tensor_f64_data(p)  # device -> host read of the result
+        ok = bool(d) and st.value == 0
+        lib.ndt_tensor_f64_release(p)
+        lib.ndt_tensor_f64_release(t)
+        return ok
+
+    for _ in range(3):
+        e2e_step()
+    e2e_steps = max(5, min(args.steps, 40))
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    w0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        assert e2e_step()
+    torch.cuda.synchronize()
+    w = torch.tensor([time.perf_counter() - w0], device="cuda")
+    if pg:
+        pg.all_reduce(w, op=pg.ReduceOp.MAX)
+    e2e = {"value": BYTES_F64 * e2e_steps * world / float(w.item()) / 1e9, "unit": "GB/s",
+           "h2d_bytes_per_step": NELEM * 8, "d2h_bytes_per_step": NELEM * 8,
+           "path": "ndt_tensor_f64_from_data (pinned host) -> ndt_tensor_f64_permutedims -> ndt_tensor_f64_data"}
+
+    # ---- extras: complex permute and the dense f64 MPS merge (DMMA GEMM)
+    extras = []
+    if not args.no_extras:
+        extras = run_extras(args, torch, lib, ndt, stream, peaks)
+
+    # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
+    cpu = None
+    if rank == 0 and world == 1:
+        t_cpu = cpu_permute_time(1)
+        cpu = {"value": BYTES_F64 / t_cpu / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": "one full 16^6 f64 tensor, GenericBackend::permute_into restated in C (oracle), 1 thread"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f64",
+            "data": "synthetic (seeded N(0,1), torch generator on device)",
+            "config": {"workload": "permutedims 16^6 f64 perm (5,3,1,0,4,2)", "batch": B,
+                       "parallelism": f"replicas x{world}",
+                       "l2": f"inputs larger than L2: {B} distinct 134 MB tensors per step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic("permute_16p6_f64"),
+                         "kernel": "permute_tiled_kernel<8>", "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
+                         "algorithmic_bytes_per_launch": BYTES_F64},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": sampler.result(),
+            "contraction": extras,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def run_extras(args, torch, lib, ndt, stream, peaks):
+    out = []
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    # complex128 permute of the same shape
+    src = torch.randn(4, NELEM, dtype=torch.complex128, device="cuda")
+    dst = torch.empty_like(src)
+    shape_c = (ctypes.c_size_t * 6)(*SHAPE)
+    perm_c = (ctypes.c_size_t * 6)(*PERM)
+
+    def cstep():
+        for i in range(src.shape[0]):
+            lib.ndt_b200_permutedims_dev(1, ctypes.c_void_p(src[i].data_ptr()), ctypes.c_void_p(dst[i].data_ptr()),
+                                         shape_c, 6, perm_c, 6, sptr)
+
+    for _ in range(3):
+        cstep()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 10
+    e0.record()
+    for _ in range(reps):
+        cstep()
+    e1.record()
+    torch.cuda.synchronize()
+    per = e0.elapsed_time(e1) / (reps * src.shape[0])
+    gbs = 2 * NELEM * 16 / (per * 1e-3) / 1e9
+    out.append({"workload": "permutedims 16^6 c128 perm (5,3,1,0,4,2)", "value": gbs, "unit": "GB/s",
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                             "frac": gbs / peaks["hbm_gbs"], "traffic": ncu_traffic("permute_16p6_c128")}})
+    del src, dst
+    # dense f64 MPS merge: A[256,4,256] x B[256,4,256] (labels (1,2,-1),(-1,3,4)) as one DMMA GEMM
+    m, n, k = 1024, 1024, 256
+    A = torch.randn(m * k, dtype=torch.float64, device="cuda")
+    Bt = torch.randn(k * n, dtype=torch.float64, device="cuda")
+    Ct = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.float64, device="cuda")
+
+    def g():
+        st = lib.ndt_b200_gemm_dev(0, m, n, k, ctypes.c_void_p(A.data_ptr()), m, 0, ctypes.c_void_p(Bt.data_ptr()),
+                                   k, 1, ctypes.c_void_p(Ct.data_ptr()), m, 0, sptr)
+        assert st == 0
+
+    for _ in range(5):
+        g()
+    times = []
+    for _ in range(50):
+        flush.zero_()  # L2 flush between timed launches (outside the events)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    t = statistics.mean(times)
+    tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
+    out.append({"workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
+                "value": tf, "unit": "TFLOP/s", "ms": t,
+                "roofline": {"bound": "fp64_tensor", "achieved": tf, "peak": FP64_DMMA_PEAK_TFLOPS, "unit": "TFLOP/s",
+                             "frac": tf / FP64_DMMA_PEAK_TFLOPS,
+                             "peak_source": "measured mma.sync.m16n8k8.f64 register-only microbenchmark"}})
+    # a large square f64 GEMM for the kernel's steady-state rate
+    m = n = k = 4096
+    A = torch.randn(m * k, dtype=torch.float64, device="cuda")
+    Bt = torch.randn(k * n, dtype=torch.float64, device="cuda")
+    Ct = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    for _ in range(2):
+        g()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(5):
+        g()
+    b.record()
+    torch.cuda.synchronize()
+    t = a.elapsed_time(b) / 5
+    tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
+    out.append({"workload": "f64 GEMM 4096^3 (DMMA kernel steady state)", "value": tf, "unit": "TFLOP/s",
+                "roofline": {"bound": "fp64_tensor", "achieved": tf, "peak": FP64_DMMA_PEAK_TFLOPS,
+                             "unit": "TFLOP/s", "frac": tf / FP64_DMMA_PEAK_TFLOPS}})
+    return out
+
+
+if __name__ == "__main__":
+    main()

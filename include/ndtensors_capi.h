@@ -1,0 +1,178 @@
+/*
+ * ndtensors_capi.h — C ABI of the B200 ndtensors library (libndtensors_capi.so).
+ *
+ * Part 1 is a drop-in for the reference's C ABI
+ * (crates/ndtensors-capi/src/lib.rs of ndtensors-rs): same 19 symbols, same
+ * signatures, same status codes, same ownership and NULL handling.  Every
+ * declaration cites the reference function it replaces.  Computation
+ * (permutedims, contract, VJP, JVP) runs on the current CUDA device; the
+ * pointers returned by *_data / *_data_mut are host pointers, as in the
+ * reference, filled from device memory on demand.
+ *
+ * Part 2 adds symbols the reference's ABI lacks (its README lists complex
+ * and block-sparse tensors as "not yet"): complex128 dense tensors, the TTGT
+ * (label-sorted) contraction, block-sparse and diag-block-sparse tensors,
+ * device-pointer interop, and stream / diagnostics control.  They follow the
+ * same conventions.  Complex values are interleaved (re, im) doubles.
+ *
+ * Threading: like the reference (Rc-based, not Send), a handle must not be
+ * used from two threads at once.  Work is issued on one CUDA stream per
+ * device (replaceable with ndt_b200_set_stream).
+ */
+#ifndef NDTENSORS_CAPI_H
+#define NDTENSORS_CAPI_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes: capi/lib.rs:17-25 */
+#define NDT_SUCCESS 0
+#define NDT_INVALID_ARGUMENT (-1)
+#define NDT_SHAPE_MISMATCH (-2)
+#define NDT_INDEX_OUT_OF_BOUNDS (-3)
+#define NDT_INTERNAL_ERROR (-4)
+#define NDT_INVALID_PERMUTATION (-5)
+
+/* Opaque handles (capi/lib.rs:28-65) */
+typedef struct ndt_tensor_f64 ndt_tensor_f64;
+typedef struct ndt_tensor_c64 ndt_tensor_c64;
+typedef struct ndt_blocksparse_f64 ndt_blocksparse_f64;
+typedef struct ndt_blocksparse_c64 ndt_blocksparse_c64;
+typedef struct ndt_diagblocksparse_f64 ndt_diagblocksparse_f64;
+typedef struct ndt_diagblocksparse_c64 ndt_diagblocksparse_c64;
+
+/* ======================= Part 1: the reference's f64 ABI ======================= */
+
+/* capi/lib.rs:81  ndt_tensor_f64_zeros */
+ndt_tensor_f64* ndt_tensor_f64_zeros(const size_t* shape, size_t ndim, int* status);
+/* capi/lib.rs:138 ndt_tensor_f64_ones */
+ndt_tensor_f64* ndt_tensor_f64_ones(const size_t* shape, size_t ndim, int* status);
+/* capi/lib.rs:195 ndt_tensor_f64_rand  (uniform [0,1)) */
+ndt_tensor_f64* ndt_tensor_f64_rand(const size_t* shape, size_t ndim, int* status);
+/* capi/lib.rs:252 ndt_tensor_f64_randn (standard normal) */
+ndt_tensor_f64* ndt_tensor_f64_randn(const size_t* shape, size_t ndim, int* status);
+/* capi/lib.rs:307 ndt_tensor_f64_from_data (copies; len must be max(1, prod(shape))) */
+ndt_tensor_f64* ndt_tensor_f64_from_data(const double* data, size_t len, const size_t* shape, size_t ndim,
+                                         int* status);
+/* capi/lib.rs:364 ndt_tensor_f64_release (NULL-safe) */
+void ndt_tensor_f64_release(ndt_tensor_f64* tensor);
+/* capi/lib.rs:374 ndt_tensor_f64_clone (shares storage, copy on write) */
+ndt_tensor_f64* ndt_tensor_f64_clone(const ndt_tensor_f64* src);
+/* capi/lib.rs:394 ndt_tensor_f64_ndim */
+size_t ndt_tensor_f64_ndim(const ndt_tensor_f64* tensor);
+/* capi/lib.rs:408 ndt_tensor_f64_len (storage length, max(1, prod(shape))) */
+size_t ndt_tensor_f64_len(const ndt_tensor_f64* tensor);
+/* capi/lib.rs:429 ndt_tensor_f64_shape */
+int ndt_tensor_f64_shape(const ndt_tensor_f64* tensor, size_t* out);
+/* capi/lib.rs:454 ndt_tensor_f64_data (host pointer, valid until mutation / release) */
+const double* ndt_tensor_f64_data(const ndt_tensor_f64* tensor);
+/* capi/lib.rs:471 ndt_tensor_f64_data_mut (copy on write; host pointer) */
+double* ndt_tensor_f64_data_mut(ndt_tensor_f64* tensor);
+/* capi/lib.rs:489 ndt_tensor_f64_get_linear */
+int ndt_tensor_f64_get_linear(const ndt_tensor_f64* tensor, size_t index, double* out);
+/* capi/lib.rs:514 ndt_tensor_f64_set_linear */
+int ndt_tensor_f64_set_linear(ndt_tensor_f64* tensor, size_t index, double value);
+/* capi/lib.rs:539 ndt_tensor_f64_fill */
+int ndt_tensor_f64_fill(ndt_tensor_f64* tensor, double value);
+/* capi/lib.rs:567 ndt_tensor_f64_permutedims (perm[i] = source axis of output axis i) */
+ndt_tensor_f64* ndt_tensor_f64_permutedims(const ndt_tensor_f64* tensor, const size_t* perm, size_t ndim,
+                                           int* status);
+/* capi/lib.rs:627 ndt_tensor_f64_contract (naive-loop semantics: output axes are
+ * A's positive labels then B's, unsorted; scalar result has shape [1]) */
+ndt_tensor_f64* ndt_tensor_f64_contract(const ndt_tensor_f64* a, const long* labels_a, size_t ndim_a,
+                                        const ndt_tensor_f64* b, const long* labels_b, size_t ndim_b,
+                                        int* status);
+/* capi/lib.rs:705 ndt_tensor_f64_contract_vjp */
+void ndt_tensor_f64_contract_vjp(const ndt_tensor_f64* a, const long* labels_a, size_t ndim_a,
+                                 const ndt_tensor_f64* b, const long* labels_b, size_t ndim_b,
+                                 const ndt_tensor_f64* grad_output, ndt_tensor_f64** grad_a_out,
+                                 ndt_tensor_f64** grad_b_out, int* status);
+/* capi/lib.rs:810 ndt_tensor_f64_contract_jvp */
+void ndt_tensor_f64_contract_jvp(const ndt_tensor_f64* a, const long* labels_a, size_t ndim_a,
+                                 const ndt_tensor_f64* b, const long* labels_b, size_t ndim_b,
+                                 const ndt_tensor_f64* tangent_a, const ndt_tensor_f64* tangent_b,
+                                 ndt_tensor_f64** primal_out, ndt_tensor_f64** tangent_out, int* status);
+
+/* ============================ Part 2: additive ============================ */
+
+/* TTGT contraction with the reference's contract_gemm semantics
+ * (crates/ndtensors/src/contract/gemm.rs:47-95): output axes sorted by label.
+ * Status: any TensorError -> NDT_SHAPE_MISMATCH, panic -> NDT_INTERNAL_ERROR. */
+ndt_tensor_f64* ndt_tensor_f64_contract_gemm(const ndt_tensor_f64* a, const long* labels_a, size_t ndim_a,
+                                             const ndt_tensor_f64* b, const long* labels_b, size_t ndim_b,
+                                             int* status);
+
+/* Complex128 dense tensors; element i is (data[2i], data[2i+1]).  Same
+ * semantics as the f64 functions of the same name (the reference's generic
+ * Tensor<c64>: tensor.rs, permutedims.rs, naive.rs, gemm.rs). */
+ndt_tensor_c64* ndt_tensor_c64_zeros(const size_t* shape, size_t ndim, int* status);
+ndt_tensor_c64* ndt_tensor_c64_ones(const size_t* shape, size_t ndim, int* status);
+ndt_tensor_c64* ndt_tensor_c64_from_data(const double* data_interleaved, size_t len, const size_t* shape,
+                                         size_t ndim, int* status);
+void ndt_tensor_c64_release(ndt_tensor_c64* tensor);
+ndt_tensor_c64* ndt_tensor_c64_clone(const ndt_tensor_c64* src);
+size_t ndt_tensor_c64_ndim(const ndt_tensor_c64* tensor);
+size_t ndt_tensor_c64_len(const ndt_tensor_c64* tensor);
+int ndt_tensor_c64_shape(const ndt_tensor_c64* tensor, size_t* out);
+const double* ndt_tensor_c64_data(const ndt_tensor_c64* tensor);
+double* ndt_tensor_c64_data_mut(ndt_tensor_c64* tensor);
+int ndt_tensor_c64_get_linear(const ndt_tensor_c64* tensor, size_t index, double* re, double* im);
+int ndt_tensor_c64_set_linear(ndt_tensor_c64* tensor, size_t index, double re, double im);
+int ndt_tensor_c64_fill(ndt_tensor_c64* tensor, double re, double im);
+ndt_tensor_c64* ndt_tensor_c64_permutedims(const ndt_tensor_c64* tensor, const size_t* perm, size_t ndim,
+                                           int* status);
+ndt_tensor_c64* ndt_tensor_c64_contract(const ndt_tensor_c64* a, const long* labels_a, size_t ndim_a,
+                                        const ndt_tensor_c64* b, const long* labels_b, size_t ndim_b,
+                                        int* status);
+ndt_tensor_c64* ndt_tensor_c64_contract_gemm(const ndt_tensor_c64* a, const long* labels_a, size_t ndim_a,
+                                             const ndt_tensor_c64* b, const long* labels_b, size_t ndim_b,
+                                             int* status);
+
+/* Device-pointer interop (the device-pointer ABI proposed in the reference's
+ * README, "CUDA support" section).  from_device_ptr copies `len` elements from
+ * device memory of the current device; device_ptr returns the tensor's device
+ * buffer (valid until mutation / release; work on it is ordered on the
+ * library stream). */
+ndt_tensor_f64* ndt_tensor_f64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
+                                               int* status);
+const double* ndt_tensor_f64_device_ptr(const ndt_tensor_f64* tensor);
+ndt_tensor_c64* ndt_tensor_c64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
+                                               int* status);
+const double* ndt_tensor_c64_device_ptr(const ndt_tensor_c64* tensor);
+
+/* Raw device kernels, no handles, no allocation by the library.
+ * dtype: 0 = f64, 1 = complex128.  `stream` is a cudaStream_t (NULL = the
+ * library stream). */
+/* permutedims into a caller buffer: dst has shape perm.map(shape)
+ * (operations/permutedims.rs:51-68, backend/generic.rs:15-39). */
+int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t* shape, size_t ndim,
+                             const size_t* perm, size_t nperm, void* stream);
+/* C (m x n, column-major, ldc) (+)= A B on FP64 tensor cores.  A is m x k:
+ * element (i,l) at A[i + l*lda] (a_kmajor = 0) or A[l + i*lda] (a_kmajor = 1);
+ * B is k x n: element (l,j) at B[l + j*ldb] (b_kmajor = 1) or B[j + l*ldb]
+ * (b_kmajor = 0).  Stands in for faer's matmul (contract/gemm.rs:209-216). */
+int ndt_b200_gemm_dev(int dtype, long m, long n, long k, const void* A, long lda, int a_kmajor, const void* B,
+                      long ldb, int b_kmajor, void* C, long ldc, int accumulate, void* stream);
+
+/* Library control and diagnostics */
+int ndt_b200_device_available(void);
+int ndt_b200_set_stream(void* stream); /* NULL restores the library's own stream */
+void* ndt_b200_get_stream(void);
+int ndt_b200_synchronize(void);
+const char* ndt_b200_last_error(void); /* text of the last failure on this thread */
+unsigned long long ndt_b200_launch_count(void); /* kernels launched by this library */
+void ndt_b200_empty_cache(void);
+
+#ifdef __cplusplus
+}
+#endif
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+#endif

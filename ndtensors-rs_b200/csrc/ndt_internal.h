@@ -1,0 +1,202 @@
+// Internal declarations of the B200 ndtensors library (libndtensors_capi.so).
+//
+// Layout of the library:
+//   device.cpp       per-device context: compute / upload streams, stream-ordered
+//                    device pool, pinned host cache, last-error text
+//   tensor.cpp       Storage (device buffer + lazily synced host mirror, copy on
+//                    write) and the dense tensor value type
+//   capi_dense.cpp   ndt_tensor_f64_* (the reference's C ABI) and ndt_tensor_c64_*
+//   permute.cu       strided gather / permutedims kernels and their planner
+//   gemm.cu          FP64 tensor-core (DMMA) GEMM: dense and grouped, f64 and c128
+//   contract.cpp     label planning (naive ABI semantics and TTGT semantics),
+//                    contraction driver, VJP / JVP compositions
+//   elementwise.cu   fill, add, diagonal scaling
+//   blocksparse.cpp  block-sparse and diag-block-sparse tensors, block-pair
+//                    table, grouped contraction, ABI exports
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+namespace ndt {
+
+// ---------------------------------------------------------------- errors
+// Error kinds mirror the reference's TensorError variants plus a "panic"
+// kind for the places where the reference panics (its C ABI's catch_unwind
+// maps those to NDT_INTERNAL_ERROR).  Each ABI entry point maps kinds onto
+// status codes exactly as crates/ndtensors-capi/src/lib.rs does.
+enum class ErrKind {
+  WrongNumberOfIndices,
+  ShapeMismatch,
+  InvalidPermutation,
+  BlockNotFound,
+  IndexOutOfBounds,
+  InvalidArgument,
+  Panic,  // reference would panic (division by zero extent, failed assert, ...)
+  Cuda,   // CUDA runtime failure or no device
+};
+
+struct Error : std::runtime_error {
+  ErrKind kind;
+  Error(ErrKind k, const std::string& m) : std::runtime_error(m), kind(k) {}
+};
+
+[[noreturn]] void throw_cuda(cudaError_t e, const char* what, const char* file, int line);
+#define NDT_CUDA(x)                                                   \
+  do {                                                                \
+    cudaError_t _e = (x);                                             \
+    if (_e != cudaSuccess) ::ndt::throw_cuda(_e, #x, __FILE__, __LINE__); \
+  } while (0)
+
+void set_last_error(const std::string& msg);
+const char* last_error();
+
+// ----------------------------------------------------------------- dtypes
+enum class DType : int { F64 = 0, C128 = 1 };
+inline size_t esize(DType t) { return t == DType::F64 ? 8 : 16; }
+
+// --------------------------------------------------------------- devices
+bool device_available();
+int current_device();  // throws ErrKind::Cuda when no device is present
+struct DeviceCtx {
+  int device = -1;
+  cudaStream_t compute = nullptr;  // all kernels of the library
+  cudaStream_t own_compute = nullptr;  // the library's own compute stream
+  cudaStream_t upload = nullptr;   // host->device copies of caller data
+  bool external_stream = false;    // compute stream supplied by the caller
+  int sm_count = 0;
+  size_t smem_optin = 0;
+};
+DeviceCtx& ctx(int device);
+DeviceCtx& ctx();  // current device
+// Device memory: stream-ordered allocations from the device's default pool
+// (release threshold raised so freed blocks are reused, not returned).
+void* dev_alloc(size_t bytes, int device);
+void dev_free(void* p, int device);
+// Pinned host memory with a size-bucketed cache (host mirrors, staging).
+void* pinned_alloc(size_t bytes, bool* pinned);
+void pinned_free(void* p, size_t bytes, bool pinned);
+void empty_caches();
+
+// ---------------------------------------------------------------- storage
+// One buffer of `len` elements.  The device buffer is authoritative once a
+// device op has produced it; the host mirror is filled on demand (data(),
+// get_linear) and stays valid until the next mutation.  A storage can also be
+// "uniform": every element equal to `fill` and nothing materialised yet
+// (zeros / ones / fill are lazy).
+struct Storage {
+  DType dt;
+  size_t len = 0;  // elements (max(1, prod(shape)) for dense tensors)
+  int device = -1;
+  void* dev = nullptr;
+  void* host = nullptr;
+  bool host_pinned = false;
+  bool dev_valid = false;
+  bool host_valid = false;
+  bool host_external = false;  // a mutable host pointer was handed out
+  bool uniform = false;        // all elements == fill, not materialised
+  double fill_re = 0.0, fill_im = 0.0;
+
+  Storage(DType t, size_t n) : dt(t), len(n) {}
+  ~Storage();
+  Storage(const Storage&) = delete;
+  Storage& operator=(const Storage&) = delete;
+
+  size_t bytes() const { return len * esize(dt); }
+  // Host view: materialises and downloads as needed.
+  void* host_read();
+  // Host view for mutation: invalidates the device copy.
+  void* host_write();
+  // Device view for reading by a kernel on the compute stream.
+  const void* dev_read();
+  // Device view for a kernel that overwrites every element.
+  void* dev_overwrite();
+  void set_uniform(double re, double im);
+  std::shared_ptr<Storage> clone() const;
+};
+
+struct Dense {
+  DType dt = DType::F64;
+  std::vector<size_t> shape;
+  std::shared_ptr<Storage> st;
+  size_t len() const { return st ? st->len : 0; }
+  size_t ndim() const { return shape.size(); }
+  void make_unique();  // copy on write (Rc::make_mut)
+};
+
+size_t prod(const std::vector<size_t>& v);
+size_t prod_max1(const std::vector<size_t>& v);
+std::vector<size_t> col_major_strides(const std::vector<size_t>& shape);
+
+Dense make_uniform(DType dt, const std::vector<size_t>& shape, double re, double im);
+Dense make_from_host(DType dt, const void* data, size_t len, const std::vector<size_t>& shape);
+Dense make_from_device(DType dt, const void* dptr, size_t len, const std::vector<size_t>& shape);
+Dense make_empty_device(DType dt, const std::vector<size_t>& shape);  // uninitialised device buffer
+
+// ------------------------------------------------------------- operations
+// Strided gather: dst (dense, column-major, shape `shape`) receives
+// src[sum_i idx_i * src_strides[i]].  Covers permutedims (strides = permuted
+// source strides), TTGT operand packing and axes pinned at index 0.
+struct GatherDesc {
+  std::vector<size_t> shape;        // destination extents
+  std::vector<int64_t> src_strides; // in elements, per destination axis
+};
+void gather(DType dt, const void* src, void* dst, const GatherDesc& g, cudaStream_t s);
+// Number of device kernels launched by this library since load (for benches).
+uint64_t launch_count();
+void count_launch();
+
+// Dense permutedims with the reference's validation (permutedims.rs:51-68).
+Dense permutedims(const Dense& t, const std::vector<size_t>& perm);
+
+// GEMM on device: C[m,n] (+)= sum_k A(i,l) * B(l,j).  A is MN-major
+// (A[i + l*lda]) or K-major (A[l + i*lda]); B is K-major (B[l + j*ldb]) or
+// MN-major (B[j + l*ldb]); C is column-major with leading dimension ldc.
+struct GemmOperand {
+  const void* ptr;
+  int64_t ld;
+  bool kmajor;
+};
+void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand B, void* C,
+          int64_t ldc, bool accumulate, cudaStream_t s);
+
+// Grouped GEMM over a device-side table.  Each problem is one output block
+// C_p (m_p x n_p, column-major, packed) = sum over its segments s of
+// A_s (m_p x k_s) * B_s (k_s x n_p).  All operands of one call share the
+// majorness flags.  Host arrays are uploaded into `scratch`-owned buffers.
+struct GroupedProblem {
+  int64_t m, n;
+  int64_t c_off;     // element offset of C block
+  int64_t seg_begin; // first segment
+  int64_t seg_count;
+};
+struct GroupedSegment {
+  int64_t a_off, b_off;  // element offsets into A / B data
+  int64_t k;
+  int64_t lda, ldb;
+  int64_t scale_off;     // offset into the k-scale vector, or -1
+};
+void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor, bool b_kmajor,
+                  const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
+                  const void* kscale, cudaStream_t s);
+
+// Elementwise helpers
+void fill_device(DType dt, void* p, size_t n, double re, double im, cudaStream_t s);
+void add_device(DType dt, const void* a, const void* b, void* c, size_t n, cudaStream_t s);
+void scale_device(DType dt, const void* a, void* c, size_t n, double re, double im, cudaStream_t s);
+
+// Contractions
+enum class ContractSemantics { Naive, Gemm };
+Dense contract(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
+               const std::vector<int32_t>& lb, ContractSemantics sem);
+void contract_vjp(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
+                  const std::vector<int32_t>& lb, const Dense& grad, Dense* ga, Dense* gb);
+Dense add(const Dense& a, const Dense& b);  // apply_binary(+) semantics
+
+}  // namespace ndt

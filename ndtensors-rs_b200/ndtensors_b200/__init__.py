@@ -1,0 +1,52 @@
+"""B200 implementation of ndtensors' contraction hot path (Python host side).
+
+The compute lives in libndtensors_capi.so (C++ / CUDA for sm_100a); this
+package binds its C ABI with ctypes and mirrors the reference's Python API
+(TensorF64, contract, contract_vjp, contract_jvp) plus complex128 and
+block-sparse tensors.
+"""
+
+from ._lib import get_lib, last_error, lib_path
+from .ops import contract, contract_gemm, contract_jvp, contract_vjp
+from .tensor import NDTensorsError, StatusCode, TensorC64, TensorF64, check_status
+
+
+def device_available() -> bool:
+    return bool(get_lib().ndt_b200_device_available())
+
+
+def synchronize() -> None:
+    check_status(get_lib().ndt_b200_synchronize(), "synchronize")
+
+
+def launch_count() -> int:
+    """Kernels launched by the library since it was loaded."""
+    return int(get_lib().ndt_b200_launch_count())
+
+
+def set_stream(stream_ptr) -> None:
+    """Run the library's kernels on a caller CUDA stream (e.g.
+    ``torch.cuda.current_stream().cuda_stream``); ``None`` restores its own."""
+    import ctypes
+
+    check_status(get_lib().ndt_b200_set_stream(ctypes.c_void_p(stream_ptr) if stream_ptr else None), "set_stream")
+
+
+__all__ = [
+    "TensorF64",
+    "TensorC64",
+    "contract",
+    "contract_gemm",
+    "contract_vjp",
+    "contract_jvp",
+    "NDTensorsError",
+    "StatusCode",
+    "check_status",
+    "get_lib",
+    "lib_path",
+    "last_error",
+    "device_available",
+    "synchronize",
+    "launch_count",
+    "set_stream",
+]
