@@ -233,7 +233,9 @@ def main():
     import ndtensors_b200 as ndt
 
     lib = ndt.get_lib()
-    stream = torch.cuda.current_stream()
+    # one dedicated stream: the library's kernels and the timing events share it
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     ndt.set_stream(stream.cuda_stream)
 
     # ---- inputs resident in HBM: `batch` distinct tensors (seeded)
@@ -381,8 +383,9 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
 
     def cstep():
         for i in range(src.shape[0]):
-            lib.ndt_b200_permutedims_dev(1, ctypes.c_void_p(src[i].data_ptr()), ctypes.c_void_p(dst[i].data_ptr()),
-                                         shape_c, 6, perm_c, 6, sptr)
+            st = lib.ndt_b200_permutedims_dev(1, ctypes.c_void_p(src[i].data_ptr()),
+                                              ctypes.c_void_p(dst[i].data_ptr()), shape_c, 6, perm_c, 6, sptr)
+            assert st == 0, ndt.last_error()
 
     for _ in range(3):
         cstep()

@@ -147,8 +147,8 @@ ndt_tensor_c64* ndt_tensor_c64_from_device_ptr(const double* dptr, size_t len, c
 const double* ndt_tensor_c64_device_ptr(const ndt_tensor_c64* tensor);
 
 /* Raw device kernels, no handles, no allocation by the library.
- * dtype: 0 = f64, 1 = complex128.  `stream` is a cudaStream_t (NULL = the
- * library stream). */
+ * dtype: 0 = f64, 1 = complex128.  `stream` is a cudaStream_t; NULL is the
+ * legacy default stream, as everywhere in CUDA. */
 /* permutedims into a caller buffer: dst has shape perm.map(shape)
  * (operations/permutedims.rs:51-68, backend/generic.rs:15-39). */
 int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t* shape, size_t ndim,

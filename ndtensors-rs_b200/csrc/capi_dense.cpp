@@ -534,7 +534,8 @@ int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t
     for (size_t x : sh)
       if (x == 0) return NDT_INTERNAL_ERROR;  // the reference panics on zero extents
     DType dt = dtype ? DType::C128 : DType::F64;
-    cudaStream_t s = stream ? (cudaStream_t)stream : ctx().compute;
+    cudaStream_t s = (cudaStream_t)stream;  // NULL = the legacy default stream, as in CUDA
+    ctx();
     std::vector<size_t> ss = col_major_strides(sh);
     GatherDesc g;
     for (size_t i = 0; i < ndim; i++) {
@@ -558,7 +559,8 @@ int ndt_b200_gemm_dev(int dtype, long m, long n, long k, const void* A, long lda
                       long ldb, int b_kmajor, void* C, long ldc, int accumulate, void* stream) {
   if (!A || !B || !C || m < 0 || n < 0 || k < 0 || (dtype != 0 && dtype != 1)) return NDT_INVALID_ARGUMENT;
   try {
-    cudaStream_t s = stream ? (cudaStream_t)stream : ctx().compute;
+    cudaStream_t s = (cudaStream_t)stream;  // NULL = the legacy default stream, as in CUDA
+    ctx();
     gemm(dtype ? DType::C128 : DType::F64, m, n, k, GemmOperand{A, lda, a_kmajor != 0},
          GemmOperand{B, ldb, b_kmajor != 0}, C, ldc, accumulate != 0, s);
     return NDT_SUCCESS;

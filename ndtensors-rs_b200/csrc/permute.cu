@@ -357,13 +357,10 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
     *ok = false;
     return;
   }
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[E == 16]) {
-    NDT_CUDA(cudaFuncSetAttribute(permute_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)c.smem_optin));
-    attr_set[E == 16] = true;
-  }
-  int per_sm = std::max(1, std::min(8, (int)(200 * 1024 / smem)));
+  NDT_CUDA(cudaFuncSetAttribute(permute_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, permute_tiled_kernel<E>, kThreads, smem));
+  per_sm = std::max(1, per_sm);
   int grid = grid_for(ntiles, per_sm, c);
   using T = typename ElemT<E>::type;
   permute_tiled_kernel<E><<<grid, kThreads, smem, s>>>((const T*)src, (T*)dst, tp);

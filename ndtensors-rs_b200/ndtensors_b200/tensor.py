@@ -85,9 +85,9 @@ class _DenseBase:
 
     @classmethod
     def from_numpy(cls, arr: np.ndarray):
-        arr = np.asfortranarray(np.asarray(arr, dtype=cls._np_dtype))
-        shape = arr.shape
-        flat = arr.ravel(order="F")
+        arr = np.asarray(arr, dtype=cls._np_dtype)
+        shape = arr.shape  # before asfortranarray, which turns 0-d into shape (1,)
+        flat = np.asfortranarray(arr).ravel(order="F")
         if flat.size == 0:
             flat = np.zeros(1, dtype=cls._np_dtype)  # storage holds max(1, prod) elements
         buf = np.ascontiguousarray(flat).view(np.float64)

@@ -19,13 +19,18 @@ def _rand(rng, shape, cplx):
     return rng.standard_normal(shape)
 
 
+def _bits(x):
+    """Raw bit pattern in column-major order (bit-exact comparison)."""
+    return np.ascontiguousarray(np.asarray(x).ravel(order="F")).view(np.uint64)
+
+
 def _check(gpu, oracle, a, perm):
     cls = gpu.TensorC64 if np.iscomplexobj(a) else gpu.TensorF64
     got = cls.from_numpy(a).permutedims(perm).to_numpy()
     st, ref = oracle.permutedims(a, perm)
     assert st == 0
     assert got.shape == ref.shape
-    assert np.array_equal(got.view(np.uint64), ref.view(np.uint64)), "permute must be bit-exact"
+    assert np.array_equal(_bits(got), _bits(ref)), "permute must be bit-exact"
 
 
 SHAPES = [
@@ -92,10 +97,10 @@ def test_permute_16pow6_full_size(gpu, oracle, cplx):
     got = p.to_numpy()
     st, ref = oracle.permutedims(a, perm)
     assert st == 0
-    assert np.array_equal(got.view(np.uint64), ref.view(np.uint64))
+    assert np.array_equal(_bits(got), _bits(ref))
     inv = tuple(int(i) for i in np.argsort(perm))
     back = p.permutedims(inv).to_numpy()
-    assert np.array_equal(back.view(np.uint64), np.asfortranarray(a).view(np.uint64))
+    assert np.array_equal(_bits(back), _bits(a))
 
 
 def test_permute_raw_device_entry(gpu, oracle):
