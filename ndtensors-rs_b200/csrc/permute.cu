@@ -11,9 +11,13 @@
 //            a tile of P x Q elements is staged through shared memory.  P
 //            spans a contiguous run of the source (G_in axes), Q a contiguous
 //            run of the destination (G_out axes), so both the global loads and
-//            the global stores are coalesced; the shared-memory row pitch is
-//            odd (in elements) so that both phases are bank-conflict free.
-//            CTAs are persistent and walk the tile list.
+//            the global stores are coalesced (512-byte runs).  The tile
+//            geometry is fixed at compile time (64 x 64 f64, 32 x 64 c128),
+//            so no integer division runs per element.  CTAs are persistent
+//            and double-buffered: the next tile is copied global -> shared
+//            with cp.async (no register staging) while the current one is
+//            written out; the odd shared-memory row pitch keeps both phases
+//            bank-conflict free.
 //   generic  anything else (broadcast / pinned axes without a stride-1
 //            source axis, short rows): one destination element per thread.
 #include <algorithm>
@@ -29,6 +33,7 @@ constexpr int kMaxGroup = 8;   // axes per tile group
 constexpr int kMaxOuter = 24;  // outer (tile-index) dims
 constexpr int kMaxGen = 24;    // axes of the generic kernel
 constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
 
 struct alignas(16) C128 {
   double re, im;
@@ -39,18 +44,21 @@ struct ElemT;
 template <>
 struct ElemT<8> {
   using type = double;
+  static constexpr int TP = 64;  // tile extent along the source-contiguous run
+  static constexpr int TQ = 64;  // tile extent along the destination-contiguous run
 };
 template <>
 struct ElemT<16> {
   using type = C128;
+  static constexpr int TP = 32;
+  static constexpr int TQ = 64;
 };
 
 struct TileParams {
-  int P, Q;    // full tile extents (elements)
-  int lds;     // shared-memory row pitch (elements), odd
+  int P, Q;  // full tile extents (elements), P <= TP, Q <= TQ
   int n_gin, n_gout;
-  int gin_n[kMaxGroup];       // extents (chunk for the last) of G_in axes
-  int64_t gin_sdst[kMaxGroup];  // destination strides of G_in axes
+  int gin_n[kMaxGroup];          // extents (chunk for the last) of G_in axes
+  int64_t gin_sdst[kMaxGroup];   // destination strides of G_in axes
   int gout_n[kMaxGroup];
   int64_t gout_ssrc[kMaxGroup];  // source strides of G_out axes
   int n_outer;
@@ -61,7 +69,7 @@ struct TileParams {
   int out_chunk_dim;  // outer dim index of the G_out chunk counter, or -1
   int64_t in_total;   // full extent of the chunked G_in axis
   int64_t out_total;
-  int in_inner;       // product of the full (unchunked) G_in extents
+  int in_inner;  // product of the full (unchunked) G_in extents
   int out_inner;
   int in_chunk, out_chunk;
   int64_t ntiles;
@@ -72,15 +80,22 @@ __global__ void __launch_bounds__(kThreads) permute_tiled_kernel(const typename 
                                                                  typename ElemT<E>::type* __restrict__ dst,
                                                                  const __grid_constant__ TileParams tp) {
   using T = typename ElemT<E>::type;
+  constexpr int TP = ElemT<E>::TP, TQ = ElemT<E>::TQ;
+  constexpr int LDS = TP + 1;           // odd pitch: conflict-free column reads
+  constexpr int RROWS = TQ / kWarps;    // q rows per warp (read phase)
+  constexpr int RCH = TP / 32;          // 32-lane chunks per row
+  constexpr int WCOLS = TP / kWarps;    // p columns per warp (write phase)
+  constexpr int WCH = TQ / 32;
+  static_assert(TP % 32 == 0 && TQ % 32 == 0 && TP % kWarps == 0 && TQ % kWarps == 0, "tile geometry");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  int64_t* qoff_src = reinterpret_cast<int64_t*>(smem_raw);
-  int64_t* poff_dst = qoff_src + tp.Q;
-  __shared__ int64_t tile_src, tile_dst;
-  __shared__ int peff_s, qeff_s;
-  T* tile = reinterpret_cast<T*>(smem_raw + (((size_t)(tp.P + tp.Q) * sizeof(int64_t) + 15) & ~size_t(15)));
+  T* tile = reinterpret_cast<T*>(smem_raw);  // two buffers of TQ * LDS elements
+  __shared__ int64_t qoff_src[TQ];
+  __shared__ int64_t poff_dst[TP];
+  __shared__ int64_t tile_src[3], tile_dst[3];
+  __shared__ int peff_s[3], qeff_s[3];
 
-  // In-tile offset tables (identical for every tile).
-  for (int q = threadIdx.x; q < tp.Q; q += blockDim.x) {
+  // In-tile offset tables, identical for every tile of the launch.
+  for (int q = threadIdx.x; q < TQ; q += blockDim.x) {
     int64_t off = 0;
     int r = q;
     for (int k = 0; k < tp.n_gout; k++) {
@@ -90,7 +105,7 @@ __global__ void __launch_bounds__(kThreads) permute_tiled_kernel(const typename 
     }
     qoff_src[q] = off;
   }
-  for (int p = threadIdx.x; p < tp.P; p += blockDim.x) {
+  for (int p = threadIdx.x; p < TP; p += blockDim.x) {
     int64_t off = 0;
     int r = p;
     for (int k = 0; k < tp.n_gin; k++) {
@@ -103,93 +118,90 @@ __global__ void __launch_bounds__(kThreads) permute_tiled_kernel(const typename 
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int nwarp = blockDim.x >> 5;
 
-  for (int64_t t = blockIdx.x; t < tp.ntiles; t += gridDim.x) {
-    __syncthreads();  // previous tile fully written out; tables ready
-    if (threadIdx.x == 0) {
-      int64_t r = t, bs = 0, bd = 0;
-      int peff = tp.P, qeff = tp.Q;
-      for (int k = 0; k < tp.n_outer; k++) {
-        int64_t d = r % tp.outer_n[k];
-        r /= tp.outer_n[k];
-        bs += d * tp.outer_ssrc[k];
-        bd += d * tp.outer_sdst[k];
-        if (k == tp.in_chunk_dim) {
-          int64_t rem = tp.in_total - d * tp.in_chunk;
-          if (rem < tp.in_chunk) peff = (int)(tp.in_inner * rem);
-        }
-        if (k == tp.out_chunk_dim) {
-          int64_t rem = tp.out_total - d * tp.out_chunk;
-          if (rem < tp.out_chunk) qeff = (int)(tp.out_inner * rem);
-        }
+  // Tile bases for tile t, computed by thread 0 into slot `sl`.
+  auto bases = [&](int64_t t, int sl) {
+    int64_t r = t, bs = 0, bd = 0;
+    int peff = tp.P, qeff = tp.Q;
+    for (int k = 0; k < tp.n_outer; k++) {
+      int64_t d = r % tp.outer_n[k];
+      r /= tp.outer_n[k];
+      bs += d * tp.outer_ssrc[k];
+      bd += d * tp.outer_sdst[k];
+      if (k == tp.in_chunk_dim) {
+        int64_t rem = tp.in_total - d * tp.in_chunk;
+        if (rem < tp.in_chunk) peff = (int)(tp.in_inner * rem);
       }
-      tile_src = bs;
-      tile_dst = bd;
-      peff_s = peff;
-      qeff_s = qeff;
-    }
-    __syncthreads();
-    const int64_t bs = tile_src, bd = tile_dst;
-    const int peff = peff_s, qeff = qeff_s;
-    const T* s = src + bs;
-    T* d = dst + bd;
-    // Read phase: a warp covers 32 consecutive source elements (p) of one
-    // q-row; loads are batched before the shared-memory stores.
-    {
-      constexpr int B = 8;
-      const int nrow_chunks = (peff + 31) >> 5;
-      const int items = nrow_chunks * qeff;  // (chunk, q) pairs
-      for (int base = warp; base < items; base += nwarp * B) {
-        T v[B];
-        int pq[B];
-#pragma unroll
-        for (int j = 0; j < B; j++) {
-          int it = base + j * nwarp;
-          pq[j] = -1;
-          if (it < items) {
-            int q = it / nrow_chunks;
-            int p = ((it - q * nrow_chunks) << 5) + lane;
-            if (p < peff) {
-              v[j] = s[p + qoff_src[q]];
-              pq[j] = q * tp.lds + p;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < B; j++)
-          if (pq[j] >= 0) tile[pq[j]] = v[j];
+      if (k == tp.out_chunk_dim) {
+        int64_t rem = tp.out_total - d * tp.out_chunk;
+        if (rem < tp.out_chunk) qeff = (int)(tp.out_inner * rem);
       }
     }
-    __syncthreads();
-    // Write phase: a warp covers 32 consecutive destination elements (q) of
-    // one p-column.
-    {
-      constexpr int B = 8;
-      const int ncol_chunks = (qeff + 31) >> 5;
-      const int items = ncol_chunks * peff;
-      for (int base = warp; base < items; base += nwarp * B) {
-        T v[B];
-        int64_t o[B];
+    tile_src[sl] = bs;
+    tile_dst[sl] = bd;
+    peff_s[sl] = peff;
+    qeff_s[sl] = qeff;
+  };
+  // Read phase of tile in slot `sl`: warp w copies rows q = w, w+8, ... of
+  // the source run straight into shared memory (cp.async, no registers).
+  auto issue_reads = [&](int b, int sl) {
+    const T* s = src + tile_src[sl];
+    T* buf = tile + b * (TQ * LDS);
+    const int peff = peff_s[sl], qeff = qeff_s[sl];
 #pragma unroll
-        for (int j = 0; j < B; j++) {
-          int it = base + j * nwarp;
-          o[j] = -1;
-          if (it < items) {
-            int p = it / ncol_chunks;
-            int q = ((it - p * ncol_chunks) << 5) + lane;
-            if (q < qeff) {
-              v[j] = tile[q * tp.lds + p];
-              o[j] = q + poff_dst[p];
-            }
-          }
+    for (int i = 0; i < RROWS; i++) {
+      const int q = warp + kWarps * i;
+      const int64_t qo = qoff_src[q];
+#pragma unroll
+      for (int c = 0; c < RCH; c++) {
+        const int p = c * 32 + lane;
+        if (q < qeff && p < peff) {
+          unsigned sa = (unsigned)__cvta_generic_to_shared(buf + q * LDS + p);
+          if constexpr (E == 8)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(sa), "l"(s + qo + p));
+          else
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(s + qo + p));
         }
+      }
+    }
+  };
+
+  // Persistent loop.  Iteration k handles tile t_k in buffer k%2 with its
+  // descriptor in slot k%3: the loads of tile t_{k+1} are in flight while
+  // tile t_k is written out.  A slot is rewritten two barriers after its
+  // last reader, a buffer one barrier after.
+  int64_t t = blockIdx.x;
+  if (threadIdx.x == 0 && t < tp.ntiles) bases(t, 0);
+  __syncthreads();  // tables and slot 0 ready
+  if (t < tp.ntiles) issue_reads(0, 0);
+  asm volatile("cp.async.commit_group;\n" ::);
+  for (int k = 0; t < tp.ntiles; t += gridDim.x, k++) {
+    const int sl = k % 3, sln = (k + 1) % 3, b = k & 1;
+    const int64_t tn = t + gridDim.x;
+    if (threadIdx.x == 0 && tn < tp.ntiles) bases(tn, sln);
+    __syncthreads();  // slot sln ready; buffer b^1 no longer read
+    if (tn < tp.ntiles) issue_reads(b ^ 1, sln);
+    asm volatile("cp.async.commit_group;\n" ::);
+    asm volatile("cp.async.wait_group 1;\n" ::);
+    __syncthreads();  // tile t_k complete in buffer b
+    // Write phase: warp w stores columns p = w, w+8, ...; 32 lanes cover 32
+    // consecutive destination elements.
+    const T* buf = tile + b * (TQ * LDS);
+    T* d = dst + tile_dst[sl];
+    const int peff = peff_s[sl], qeff = qeff_s[sl];
 #pragma unroll
-        for (int j = 0; j < B; j++)
-          if (o[j] >= 0) d[o[j]] = v[j];
+    for (int i = 0; i < WCOLS; i++) {
+      const int p = warp + kWarps * i;
+      const bool pok = p < peff;
+      const int64_t po = poff_dst[p];
+#pragma unroll
+      for (int c = 0; c < WCH; c++) {
+        const int q = c * 32 + lane;
+        if (pok && q < qeff) d[po + q] = buf[q * LDS + p];
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;\n" ::);
 }
 
 struct GenParams {
@@ -239,14 +251,14 @@ template <int E>
 void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_in, cudaStream_t s,
                   const DeviceCtx& c, bool* ok) {
   const int r = (int)ax.size();
-  const int target = (E == 8) ? 64 : 32;  // P and Q targets: 512-byte runs
+  const int tP = ElemT<E>::TP, tQ = ElemT<E>::TQ;
   TileParams tp{};
   std::vector<char> used(r, 0);
   // G_out: destination axes 0, 1, ... (never the source's stride-1 axis)
   int Q = 1, nq = 0, out_chunk_axis = -1, out_chunk = 1;
   for (int i = 0; i < r && nq < kMaxGroup; i++) {
     if (i == a_in) break;
-    if ((int64_t)Q * ax[i].n <= target) {
+    if ((int64_t)Q * ax[i].n <= tQ) {
       tp.gout_n[nq] = (int)ax[i].n;
       tp.gout_ssrc[nq] = ax[i].ssrc;
       Q *= (int)ax[i].n;
@@ -254,14 +266,14 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
       nq++;
       continue;
     }
-    int c = std::max(1, target / Q);
-    if (c > 1) {
-      tp.gout_n[nq] = c;
+    int cch = std::max(1, tQ / Q);
+    if (cch > 1) {
+      tp.gout_n[nq] = cch;
       tp.gout_ssrc[nq] = ax[i].ssrc;
-      Q *= c;
+      Q *= cch;
       used[i] = 2;
       out_chunk_axis = i;
-      out_chunk = c;
+      out_chunk = cch;
       nq++;
     }
     break;
@@ -272,7 +284,7 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
   int64_t run = 1;
   while (cur >= 0 && np_ < kMaxGroup) {
     if (used[cur]) break;
-    if ((int64_t)P * ax[cur].n <= target) {
+    if ((int64_t)P * ax[cur].n <= tP) {
       tp.gin_n[np_] = (int)ax[cur].n;
       tp.gin_sdst[np_] = ax[cur].sdst;
       P *= (int)ax[cur].n;
@@ -288,23 +300,26 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
       cur = nxt;
       continue;
     }
-    int c = std::max(1, target / P);
-    if (c > 1) {
-      tp.gin_n[np_] = c;
+    int cch = std::max(1, tP / P);
+    if (cch > 1) {
+      tp.gin_n[np_] = cch;
       tp.gin_sdst[np_] = ax[cur].sdst;
-      P *= c;
+      P *= cch;
       used[cur] = 2;
       in_chunk_axis = cur;
-      in_chunk = c;
+      in_chunk = cch;
       np_++;
     }
     break;
+  }
+  if (P < 2 || Q < 2) {
+    *ok = false;
+    return;
   }
   tp.P = P;
   tp.Q = Q;
   tp.n_gin = np_;
   tp.n_gout = nq;
-  tp.lds = (P % 2 == 0) ? P + 1 : P;
   // Outer dims: chunk counters first, then the untouched axes
   int no = 0;
   tp.in_chunk_dim = tp.out_chunk_dim = -1;
@@ -318,15 +333,16 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
   };
   tp.in_inner = P / in_chunk;
   tp.out_inner = Q / out_chunk;
+  tp.in_total = 1;
+  tp.in_chunk = 1;
+  tp.out_total = 1;
+  tp.out_chunk = 1;
   if (in_chunk_axis >= 0) {
     const Ax& a = ax[in_chunk_axis];
     tp.in_chunk_dim = no;
     tp.in_total = a.n;
     tp.in_chunk = in_chunk;
     add_outer((a.n + in_chunk - 1) / in_chunk, a.ssrc * in_chunk, a.sdst * in_chunk);
-  } else {
-    tp.in_total = 1;
-    tp.in_chunk = 1;
   }
   if (out_chunk_axis >= 0) {
     const Ax& a = ax[out_chunk_axis];
@@ -334,9 +350,6 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
     tp.out_total = a.n;
     tp.out_chunk = out_chunk;
     add_outer((a.n + out_chunk - 1) / out_chunk, a.ssrc * out_chunk, a.sdst * out_chunk);
-  } else {
-    tp.out_total = 1;
-    tp.out_chunk = 1;
   }
   for (int i = 0; i < r; i++) {
     if (used[i]) continue;
@@ -348,16 +361,12 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
   }
   tp.n_outer = no;
   tp.ntiles = ntiles;
-  if (P < 2 || Q < 2) {
-    *ok = false;
-    return;
+  const size_t smem = 2 * (size_t)ElemT<E>::TQ * (ElemT<E>::TP + 1) * E;
+  static bool attr_done = false;
+  if (!attr_done) {
+    NDT_CUDA(cudaFuncSetAttribute(permute_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_done = true;
   }
-  size_t smem = (((size_t)(P + Q) * sizeof(int64_t) + 15) & ~size_t(15)) + (size_t)Q * tp.lds * E;
-  if (smem > c.smem_optin) {
-    *ok = false;
-    return;
-  }
-  NDT_CUDA(cudaFuncSetAttribute(permute_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
   NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, permute_tiled_kernel<E>, kThreads, smem));
   per_sm = std::max(1, per_sm);
