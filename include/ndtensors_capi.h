@@ -160,6 +160,23 @@ int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t
 int ndt_b200_gemm_dev(int dtype, long m, long n, long k, const void* A, long lda, int a_kmajor, const void* B,
                       long ldb, int b_kmajor, void* C, long ldc, int accumulate, void* stream);
 
+/* Dense f64 contraction that allocates no memory (no counterpart in the
+ * reference).  For callers that may not call cudaMalloc -- allocation-free
+ * hot loops, hosts that own the device memory budget, graph-oriented
+ * runtimes.  Same label semantics as ndt_tensor_f64_contract; inputs and the
+ * output are caller-owned device buffers (column-major, A and B dense over
+ * their shapes, zero extents rejected with NDT_INTERNAL_ERROR); c must hold
+ * c_len >= output length elements; out_shape (may be NULL) receives the
+ * output shape (up to ndim_a + ndim_b entries, or 1).  Operands that need
+ * packing use a fixed 16 MiB scratch array in device memory, held by every
+ * GPU that loads the library until exit; larger requests are rejected with
+ * NDT_INVALID_ARGUMENT (message in ndt_b200_last_error).  The first call on a
+ * device looks up that array's device address (make it before any stream
+ * capture).  Calls share the array: calls that overlap on the GPU race. */
+int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shape_a, size_t ndim_a, const long* labels_a,
+                                  const double* b, const size_t* shape_b, size_t ndim_b, const long* labels_b,
+                                  double* c, size_t c_len, size_t* out_shape, size_t* out_ndim, void* stream);
+
 /* Library control and diagnostics */
 int ndt_b200_device_available(void);
 int ndt_b200_set_stream(void* stream); /* NULL restores the library's own stream */

@@ -93,6 +93,12 @@ SIGNATURES = [
         [ctypes.c_int, ctypes.c_long, ctypes.c_long, ctypes.c_long, vp, ctypes.c_long, ctypes.c_int, vp,
          ctypes.c_long, ctypes.c_int, vp, ctypes.c_long, ctypes.c_int, vp],
     ),
+    (
+        "ndt_b200_contract_f64_noalloc",
+        ctypes.c_int,
+        [vp, c_size_p, ctypes.c_size_t, c_long_p, vp, c_size_p, ctypes.c_size_t, c_long_p, vp, ctypes.c_size_t,
+         c_size_p, c_size_p, vp],
+    ),
     ("ndt_b200_device_available", ctypes.c_int, []),
     ("ndt_b200_set_stream", ctypes.c_int, [vp]),
     ("ndt_b200_get_stream", vp, []),
