@@ -160,6 +160,124 @@ int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t
 int ndt_b200_gemm_dev(int dtype, long m, long n, long k, const void* A, long lda, int a_kmajor, const void* B,
                       long ldb, int b_kmajor, void* C, long ldc, int accumulate, void* stream);
 
+/* Block-sparse tensors (BlockSparseTensor, blocksparse_tensor.rs; storage in
+ * storage/blocksparse/).  Structure arguments: ndim axes; nblocks[ax] blocks
+ * on axis ax; block_sizes = the sizes of axis 0's blocks, then axis 1's, ...
+ * (BlockDim::new, block_dim.rs:45); nnzb stored blocks whose coordinates are
+ * coords[b*ndim .. b*ndim+ndim), packed in that order
+ * (BlockOffsets::from_blocks, block_offsets.rs:76-90).  Element type as the
+ * name says (c64: interleaved re/im; lengths count elements).
+ * Errors: invalid / duplicate coordinates -> NDT_INVALID_ARGUMENT, a missing
+ * block -> NDT_INDEX_OUT_OF_BOUNDS, a TensorError -> NDT_SHAPE_MISMATCH
+ * (NDT_INVALID_PERMUTATION for permutedims), a panic -> NDT_INTERNAL_ERROR. */
+/* BlockSparseTensor::zeros (blocksparse_tensor.rs:68) */
+ndt_blocksparse_f64* ndt_blocksparse_f64_zeros(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
+                                               size_t nnzb, const size_t* coords, int* status);
+/* BlockSparse::from_vec with from_blocks offsets (storage.rs:125); len = total stored elements */
+ndt_blocksparse_f64* ndt_blocksparse_f64_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
+                                                   size_t nnzb, const size_t* coords, const double* data, size_t len,
+                                                   int* status);
+void ndt_blocksparse_f64_release(ndt_blocksparse_f64* t);
+size_t ndt_blocksparse_f64_ndim(const ndt_blocksparse_f64* t);
+size_t ndt_blocksparse_f64_nnzblocks(const ndt_blocksparse_f64* t); /* nnzblocks (blocksparse_tensor.rs:99) */
+size_t ndt_blocksparse_f64_nnz(const ndt_blocksparse_f64* t);       /* nnz (blocksparse_tensor.rs:93) */
+size_t ndt_blocksparse_f64_nblocks_total(const ndt_blocksparse_f64* t); /* length of block_sizes */
+/* block dims, stored block coordinates (storage order) and packed offsets; any pointer may be NULL */
+int ndt_blocksparse_f64_structure(const ndt_blocksparse_f64* t, size_t* nblocks, size_t* block_sizes,
+                                  size_t* coords, size_t* offsets);
+/* insertblock (blocksparse_tensor.rs:210-235): len must equal the block's element count */
+int ndt_blocksparse_f64_insert_block(ndt_blocksparse_f64* t, const size_t* coords, const double* data, size_t len);
+/* blockview (blocksparse_tensor.rs:158-164): copies the block out (len >= block elements) */
+int ndt_blocksparse_f64_get_block(const ndt_blocksparse_f64* t, const size_t* coords, double* out, size_t len);
+const double* ndt_blocksparse_f64_data(const ndt_blocksparse_f64* t);       /* host view of packed data */
+const double* ndt_blocksparse_f64_device_ptr(const ndt_blocksparse_f64* t); /* device view of packed data */
+/* contract_blocksparse (contract/blocksparse.rs:87-183): one grouped FP64 tensor-core launch */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract(const ndt_blocksparse_f64* a, const long* labels_a,
+                                                  size_t ndim_a, const ndt_blocksparse_f64* b, const long* labels_b,
+                                                  size_t ndim_b, int* status);
+/* The output blocks of `rank`'s FLOP-balanced contiguous range of the sorted output block list
+ * (contract_blocksparse split over nranks processes / GPUs; no collective). */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_shard(const ndt_blocksparse_f64* a, const long* labels_a,
+                                                        size_t ndim_a, const ndt_blocksparse_f64* b,
+                                                        const long* labels_b, size_t ndim_b, int rank, int nranks,
+                                                        int* status);
+/* Host-only plan of contract_shard: output blocks and real flops per rank (either array may be NULL) */
+int ndt_blocksparse_f64_shard_plan(const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a,
+                                   const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b, int nranks,
+                                   size_t* blocks_per_rank, double* flops_per_rank);
+int ndt_blocksparse_c64_shard_plan(const ndt_blocksparse_c64* a, const long* labels_a, size_t ndim_a,
+                                   const ndt_blocksparse_c64* b, const long* labels_b, size_t ndim_b, int nranks,
+                                   size_t* blocks_per_rank, double* flops_per_rank);
+/* permutedims_blocksparse (operations/blocksparse.rs:61-129) */
+ndt_blocksparse_f64* ndt_blocksparse_f64_permutedims(const ndt_blocksparse_f64* t, const size_t* perm, size_t nperm,
+                                                     int* status);
+/* to_dense / from_dense (blocksparse_tensor.rs:290-391) */
+ndt_tensor_f64* ndt_blocksparse_f64_to_dense(const ndt_blocksparse_f64* t, int* status);
+ndt_blocksparse_f64* ndt_blocksparse_f64_from_dense(const ndt_tensor_f64* dense, size_t ndim, const size_t* nblocks,
+                                                    const size_t* block_sizes, size_t nnzb, const size_t* coords,
+                                                    int* status);
+
+/* complex128 block-sparse: same functions */
+ndt_blocksparse_c64* ndt_blocksparse_c64_zeros(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
+                                               size_t nnzb, const size_t* coords, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
+                                                   size_t nnzb, const size_t* coords, const double* data, size_t len,
+                                                   int* status);
+void ndt_blocksparse_c64_release(ndt_blocksparse_c64* t);
+size_t ndt_blocksparse_c64_ndim(const ndt_blocksparse_c64* t);
+size_t ndt_blocksparse_c64_nnzblocks(const ndt_blocksparse_c64* t);
+size_t ndt_blocksparse_c64_nnz(const ndt_blocksparse_c64* t);
+size_t ndt_blocksparse_c64_nblocks_total(const ndt_blocksparse_c64* t);
+int ndt_blocksparse_c64_structure(const ndt_blocksparse_c64* t, size_t* nblocks, size_t* block_sizes,
+                                  size_t* coords, size_t* offsets);
+int ndt_blocksparse_c64_insert_block(ndt_blocksparse_c64* t, const size_t* coords, const double* data, size_t len);
+int ndt_blocksparse_c64_get_block(const ndt_blocksparse_c64* t, const size_t* coords, double* out, size_t len);
+const double* ndt_blocksparse_c64_data(const ndt_blocksparse_c64* t);
+const double* ndt_blocksparse_c64_device_ptr(const ndt_blocksparse_c64* t);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract(const ndt_blocksparse_c64* a, const long* labels_a,
+                                                  size_t ndim_a, const ndt_blocksparse_c64* b, const long* labels_b,
+                                                  size_t ndim_b, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_shard(const ndt_blocksparse_c64* a, const long* labels_a,
+                                                        size_t ndim_a, const ndt_blocksparse_c64* b,
+                                                        const long* labels_b, size_t ndim_b, int rank, int nranks,
+                                                        int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_permutedims(const ndt_blocksparse_c64* t, const size_t* perm, size_t nperm,
+                                                     int* status);
+ndt_tensor_c64* ndt_blocksparse_c64_to_dense(const ndt_blocksparse_c64* t, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_from_dense(const ndt_tensor_c64* dense, size_t ndim, const size_t* nblocks,
+                                                    const size_t* block_sizes, size_t nnzb, const size_t* coords,
+                                                    int* status);
+
+/* DiagBlockSparse tensors (diagblocksparse.rs, diagblocksparse_tensor.rs): only
+ * the min(block shape) diagonal values of each listed block, packed in the
+ * listed order (diagblocksparse.rs:86, :218-230).  The reference has no
+ * contraction for them; ndt_blocksparse_*_contract_diag defines one as the
+ * block-sparse contraction with the diagonal blocks made dense, and runs it
+ * as a fused diagonal scaling when the diagonal tensor is a rank-2 block
+ * diagonal contracted with A's last axis. */
+ndt_diagblocksparse_f64* ndt_diagblocksparse_f64_from_data(size_t ndim, const size_t* nblocks,
+                                                           const size_t* block_sizes, size_t nnzb,
+                                                           const size_t* coords, const double* diag, size_t len,
+                                                           int* status);
+void ndt_diagblocksparse_f64_release(ndt_diagblocksparse_f64* t);
+size_t ndt_diagblocksparse_f64_nnz(const ndt_diagblocksparse_f64* t);
+ndt_tensor_f64* ndt_diagblocksparse_f64_to_dense(const ndt_diagblocksparse_f64* t, int* status);
+ndt_blocksparse_f64* ndt_diagblocksparse_f64_to_blocksparse(const ndt_diagblocksparse_f64* t, int* status);
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_diag(const ndt_blocksparse_f64* a, const long* labels_a,
+                                                       size_t ndim_a, const ndt_diagblocksparse_f64* s,
+                                                       const long* labels_s, size_t ndim_s, int* status);
+ndt_diagblocksparse_c64* ndt_diagblocksparse_c64_from_data(size_t ndim, const size_t* nblocks,
+                                                           const size_t* block_sizes, size_t nnzb,
+                                                           const size_t* coords, const double* diag, size_t len,
+                                                           int* status);
+void ndt_diagblocksparse_c64_release(ndt_diagblocksparse_c64* t);
+size_t ndt_diagblocksparse_c64_nnz(const ndt_diagblocksparse_c64* t);
+ndt_tensor_c64* ndt_diagblocksparse_c64_to_dense(const ndt_diagblocksparse_c64* t, int* status);
+ndt_blocksparse_c64* ndt_diagblocksparse_c64_to_blocksparse(const ndt_diagblocksparse_c64* t, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_diag(const ndt_blocksparse_c64* a, const long* labels_a,
+                                                       size_t ndim_a, const ndt_diagblocksparse_c64* s,
+                                                       const long* labels_s, size_t ndim_s, int* status);
+
 /* Dense f64 contraction that allocates no memory (no counterpart in the
  * reference).  For callers that may not call cudaMalloc -- allocation-free
  * hot loops, hosts that own the device memory budget, graph-oriented

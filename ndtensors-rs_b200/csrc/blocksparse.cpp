@@ -1,0 +1,969 @@
+// Block-sparse and diag-block-sparse tensors and their contraction.
+//
+// Storage model of the reference (storage/blocksparse/*, blocksparse_tensor.rs):
+// per-axis block sizes (BlockDim), a list of stored blocks packed in the
+// order given (BlockOffsets::from_blocks, block_offsets.rs:76-90), each block
+// a column-major dense array.  The data lives in device memory.
+//
+// contract_blocksparse (contract/blocksparse.rs:87-275) becomes:
+//   host   validate (label counts, block counts / sizes on contracted axes),
+//          match block pairs with a hash join on the contracted coordinates
+//          (same pair set and the same (A, B) storage order as the
+//          reference's nnzA x nnzB scan), output blocks sorted
+//          lexicographically with packed offsets; per output block its
+//          pairs form the device-side table of one grouped GEMM launch;
+//   device one grouped DMMA launch (gemm.cu): a CTA owns an output tile and
+//          accumulates all matched pairs of its block in registers.
+// Operand blocks whose axes are not already [free..., contracted...] (A) /
+// [contracted..., free...] (B) are permuted block by block first (TTGT).
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <unordered_map>
+
+#include "../../include/ndtensors_capi.h"
+#include "ndt_internal.h"
+
+namespace ndt {
+
+struct BlockSparseT {
+  DType dt = DType::F64;
+  std::vector<std::vector<size_t>> bsz;     // per-axis block sizes
+  std::vector<std::vector<size_t>> coords;  // stored blocks, storage order
+  std::vector<size_t> offs;                 // packed offsets, size nnzb + 1
+  std::shared_ptr<Storage> st;
+
+  size_t ndim() const { return bsz.size(); }
+  size_t nnzb() const { return coords.size(); }
+  size_t total() const { return offs.empty() ? 0 : offs.back(); }
+  std::vector<size_t> block_shape(const std::vector<size_t>& c) const {
+    std::vector<size_t> s(c.size());
+    for (size_t i = 0; i < c.size(); i++) s[i] = bsz[i][c[i]];
+    return s;
+  }
+  size_t block_elems(const std::vector<size_t>& c) const {
+    size_t p = 1;
+    for (size_t i = 0; i < c.size(); i++) p *= bsz[i][c[i]];
+    return p;
+  }
+  size_t dense_extent(size_t ax) const {
+    size_t s = 0;
+    for (size_t x : bsz[ax]) s += x;
+    return s;
+  }
+  size_t block_start(size_t ax, size_t c) const {
+    size_t s = 0;
+    for (size_t i = 0; i < c; i++) s += bsz[ax][i];
+    return s;
+  }
+  void pack() {
+    offs.assign(coords.size() + 1, 0);
+    for (size_t b = 0; b < coords.size(); b++) offs[b + 1] = offs[b] + block_elems(coords[b]);
+  }
+  long find(const std::vector<size_t>& c) const {
+    for (size_t b = 0; b < coords.size(); b++)
+      if (coords[b] == c) return (long)b;
+    return -1;
+  }
+};
+
+struct DiagBlockSparseT {
+  BlockSparseT s;  // coords / block sizes; offs are diagonal offsets
+  size_t diag_size(const std::vector<size_t>& c) const {
+    if (c.empty()) return 0;
+    size_t m = SIZE_MAX;
+    for (size_t i = 0; i < c.size(); i++) m = std::min(m, s.bsz[i][c[i]]);
+    return m;
+  }
+};
+
+namespace {
+
+void check_structure(const std::vector<std::vector<size_t>>& bsz, const std::vector<std::vector<size_t>>& coords) {
+  if (bsz.size() > (size_t)kBsMaxRank) throw Error(ErrKind::InvalidArgument, "block-sparse rank above 16");
+  std::map<std::vector<size_t>, int> seen;
+  for (const auto& c : coords) {
+    if (c.size() != bsz.size()) throw Error(ErrKind::InvalidArgument, "block coordinate rank mismatch");
+    for (size_t i = 0; i < c.size(); i++)
+      if (c[i] >= bsz[i].size()) throw Error(ErrKind::InvalidArgument, "block coordinate out of range");
+    if (seen[c]++) throw Error(ErrKind::InvalidArgument, "duplicate block coordinate");
+  }
+}
+
+BlockSparseT make_bs(DType dt, const std::vector<std::vector<size_t>>& bsz,
+                     const std::vector<std::vector<size_t>>& coords) {
+  check_structure(bsz, coords);
+  BlockSparseT t;
+  t.dt = dt;
+  t.bsz = bsz;
+  t.coords = coords;
+  t.pack();
+  t.st = std::make_shared<Storage>(dt, t.total());
+  t.st->set_uniform(0.0, 0.0);
+  return t;
+}
+
+// Per-block permute of a packed tensor: block b (shape sh_b) goes to the
+// same offset in dst with axes reordered by perm.
+void permute_blocks(DType dt, const void* src, void* dst, const BlockSparseT& t, const std::vector<size_t>& perm,
+                    const std::vector<size_t>& dst_offs, const std::vector<size_t>& order, cudaStream_t s) {
+  const size_t es = esize(dt);
+  for (size_t r = 0; r < order.size(); r++) {
+    size_t b = order[r];
+    std::vector<size_t> sh = t.block_shape(t.coords[b]);
+    std::vector<size_t> st = col_major_strides(sh);
+    GatherDesc g;
+    for (size_t i = 0; i < perm.size(); i++) {
+      g.shape.push_back(sh[perm[i]]);
+      g.src_strides.push_back((int64_t)st[perm[i]]);
+    }
+    const char* sp = (const char*)src + t.offs[b] * es;
+    char* dp = (char*)dst + dst_offs[r] * es;
+    if (t.block_elems(t.coords[b]) == 0) continue;
+    if (g.shape.empty()) {
+      NDT_CUDA(cudaMemcpyAsync(dp, sp, es, cudaMemcpyDeviceToDevice, s));
+    } else {
+      gather(dt, sp, dp, g, s);
+    }
+  }
+}
+
+bool is_prefix_run(const std::vector<size_t>& v, size_t start) {
+  for (size_t i = 0; i < v.size(); i++)
+    if (v[i] != start + i) return false;
+  return true;
+}
+
+}  // namespace
+
+// contract_blocksparse (contract/blocksparse.rs:87-183).  With nranks > 1 only
+// the output blocks of this rank's FLOP-balanced contiguous range of the
+// sorted output block list are computed (and stored).
+struct ShardPlan {
+  std::vector<size_t> blocks;  // output blocks per rank
+  std::vector<double> flops;   // real flop per rank
+};
+
+BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
+                         const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr) {
+  const size_t na = A.ndim(), nb = B.ndim();
+  if (A.dt != B.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
+  if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
+  if (lb.size() != nb) throw Error(ErrKind::WrongNumberOfIndices, "labels_b length != ndim(b)");
+  // ContractionProperties pairs: first match in B (properties.rs:100-111)
+  std::vector<size_t> pa, pb, ua, ub;
+  for (size_t i = 0; i < na; i++) {
+    if (la[i] >= 0) continue;
+    for (size_t j = 0; j < nb; j++)
+      if (la[i] == lb[j]) {
+        pa.push_back(i);
+        pb.push_back(j);
+        break;
+      }
+  }
+  for (size_t i = 0; i < na; i++)
+    if (std::find(pa.begin(), pa.end(), i) == pa.end()) ua.push_back(i);
+  for (size_t j = 0; j < nb; j++)
+    if (std::find(pb.begin(), pb.end(), j) == pb.end()) ub.push_back(j);
+  // blocksparse.rs:114-132: same block count and sizes on contracted axes
+  for (size_t p = 0; p < pa.size(); p++) {
+    if (A.bsz[pa[p]].size() != B.bsz[pb[p]].size()) throw Error(ErrKind::ShapeMismatch, "block counts differ");
+    for (size_t q = 0; q < A.bsz[pa[p]].size(); q++)
+      if (A.bsz[pa[p]][q] != B.bsz[pb[p]][q]) throw Error(ErrKind::ShapeMismatch, "block sizes differ");
+  }
+  // output BlockDims (blocksparse.rs:186-209)
+  BlockSparseT C;
+  C.dt = A.dt;
+  for (size_t i : ua) C.bsz.push_back(A.bsz[i]);
+  for (size_t j : ub) C.bsz.push_back(B.bsz[j]);
+  const bool scalar_out = C.bsz.empty();
+  if (scalar_out) C.bsz.push_back({1});
+  // pair scan as a hash join, preserving (A storage order, B storage order)
+  auto key_of = [](const std::vector<size_t>& c, const std::vector<size_t>& axes) {
+    std::vector<size_t> k;
+    for (size_t a : axes) k.push_back(c[a]);
+    return k;
+  };
+  std::map<std::vector<size_t>, std::vector<size_t>> bmap;
+  for (size_t b = 0; b < B.nnzb(); b++) bmap[key_of(B.coords[b], pb)].push_back(b);
+  std::map<std::vector<size_t>, std::vector<std::pair<size_t, size_t>>> contrib;  // sorted output blocks
+  for (size_t a = 0; a < A.nnzb(); a++) {
+    auto it = bmap.find(key_of(A.coords[a], pa));
+    if (it == bmap.end()) continue;
+    for (size_t b : it->second) {
+      std::vector<size_t> oc;
+      for (size_t i : ua) oc.push_back(A.coords[a][i]);
+      for (size_t j : ub) oc.push_back(B.coords[b][j]);
+      if (oc.empty()) oc.push_back(0);
+      contrib[oc].push_back({a, b});
+    }
+  }
+  // TTGT of each pair is contract_gemm on the blocks (gemm.rs:47-236):
+  // perm_b with a repeated axis is not a permutation -> InvalidPermutation.
+  {
+    std::vector<size_t> perm_b(pb);
+    perm_b.insert(perm_b.end(), ub.begin(), ub.end());
+    bool id = true;
+    for (size_t i = 0; i < perm_b.size(); i++) id &= perm_b[i] == i;
+    std::vector<char> seen(nb, 0);
+    bool valid = perm_b.size() == nb;
+    for (size_t p : perm_b) {
+      if (p >= nb || seen[p]) valid = false;
+      if (p < nb) seen[p] = 1;
+    }
+    if (!contrib.empty() && !pa.empty() && !id && !valid)
+      throw Error(ErrKind::InvalidPermutation, "contracted axes of B repeat");
+  }
+  // output label order vs contract_gemm's sorted order (properties.rs:169-186)
+  std::vector<int32_t> olab;
+  for (size_t i : ua) olab.push_back(la[i]);
+  for (size_t j : ub) olab.push_back(lb[j]);
+  std::vector<size_t> perm_c(olab.size());
+  for (size_t i = 0; i < perm_c.size(); i++) perm_c[i] = i;
+  std::stable_sort(perm_c.begin(), perm_c.end(), [&](size_t x, size_t y) { return olab[x] < olab[y]; });
+  bool permute_c = false;
+  for (size_t i = 0; i < perm_c.size(); i++)
+    if (olab[perm_c[i]] != olab[i]) permute_c = true;
+
+  // sorted output blocks; FLOP-balanced contiguous range for this rank
+  std::vector<std::vector<size_t>> all_out;
+  std::vector<double> work;
+  const double cf = A.dt == DType::C128 ? 8.0 : 2.0;
+  for (auto& kv : contrib) {
+    all_out.push_back(kv.first);
+    double w = 0;
+    for (auto& pr : kv.second) {
+      double m = 1, n = 1, k = 1;
+      for (size_t i : ua) m *= (double)A.bsz[i][A.coords[pr.first][i]];
+      for (size_t j : ub) n *= (double)B.bsz[j][B.coords[pr.second][j]];
+      for (size_t i : pa) k *= (double)A.bsz[i][A.coords[pr.first][i]];
+      w += cf * m * n * k;
+    }
+    work.push_back(w);
+  }
+  // Contiguous ranges of the sorted output blocks, cut where the running
+  // FLOP sum crosses r/nranks of the total (an output block is never split).
+  std::vector<size_t> cut(nranks + 1, all_out.size());
+  cut[0] = 0;
+  {
+    double tot = 0;
+    for (double w : work) tot += w;
+    double acc = 0;
+    int r = 1;
+    for (size_t i = 0; i < all_out.size() && r < nranks; i++) {
+      acc += work[i];
+      while (r < nranks && acc >= tot * r / nranks) cut[r++] = i + 1;
+    }
+  }
+  if (plan_only) {
+    plan_only->blocks.assign(nranks, 0);
+    plan_only->flops.assign(nranks, 0.0);
+    for (int r = 0; r < nranks; r++) {
+      plan_only->blocks[r] = cut[r + 1] - cut[r];
+      for (size_t i = cut[r]; i < cut[r + 1]; i++) plan_only->flops[r] += work[i];
+    }
+    return C;
+  }
+  const size_t lo = cut[rank], hi = cut[rank + 1];
+  for (size_t i = lo; i < hi; i++) C.coords.push_back(all_out[i]);
+  C.pack();
+  C.st = std::make_shared<Storage>(C.dt, C.total());
+  if (C.total() == 0 || contrib.empty()) {
+    C.st->set_uniform(0.0, 0.0);
+    return C;
+  }
+  // insertblock shape check for the first contribution (blocksparse_tensor.rs:218-223)
+  for (size_t ob = 0; ob < C.nnzb(); ob++) {
+    std::vector<size_t> sh = C.block_shape(C.coords[ob]);
+    if (permute_c) {
+      std::vector<size_t> sorted(sh.size());
+      for (size_t i = 0; i < sh.size(); i++) sorted[i] = sh[perm_c[i]];
+      if (sorted != sh) throw Error(ErrKind::ShapeMismatch, "contract_gemm block shape differs from output block");
+    }
+  }
+  for (size_t ob = 0; ob < C.nnzb(); ob++)
+    for (auto& pr : contrib[C.coords[ob]]) {
+      if (A.block_elems(A.coords[pr.first]) == 0 || B.block_elems(B.coords[pr.second]) == 0)
+        throw Error(ErrKind::Panic, "zero-size block in a contracted pair");
+    }
+
+  const DeviceCtx& c = ctx();
+  cudaStream_t s = c.compute;
+  const int dev = current_device();
+  const size_t es = esize(A.dt);
+  // operand layouts at the tensor level
+  const void* Ad = A.st->dev_read();
+  const void* Bd = B.st->dev_read();
+  void* Aown = nullptr;
+  void* Bown = nullptr;
+  bool a_kmajor = false, b_kmajor = true;
+  if (is_prefix_run(ua, 0) && is_prefix_run(pa, ua.size())) {
+    a_kmajor = false;
+  } else if (is_prefix_run(pa, 0) && is_prefix_run(ua, pa.size())) {
+    a_kmajor = true;
+  } else {
+    std::vector<size_t> perm(ua);
+    perm.insert(perm.end(), pa.begin(), pa.end());
+    std::vector<size_t> order(A.nnzb());
+    for (size_t i = 0; i < order.size(); i++) order[i] = i;
+    Aown = dev_alloc(A.total() * es, dev);
+    permute_blocks(A.dt, Ad, Aown, A, perm, A.offs, order, s);
+    Ad = Aown;
+    a_kmajor = false;
+  }
+  if (is_prefix_run(pb, 0) && is_prefix_run(ub, pb.size())) {
+    b_kmajor = true;
+  } else if (is_prefix_run(ub, 0) && is_prefix_run(pb, ub.size())) {
+    b_kmajor = false;
+  } else {
+    std::vector<size_t> perm(pb);
+    perm.insert(perm.end(), ub.begin(), ub.end());
+    std::vector<size_t> order(B.nnzb());
+    for (size_t i = 0; i < order.size(); i++) order[i] = i;
+    Bown = dev_alloc(B.total() * es, dev);
+    permute_blocks(B.dt, Bd, Bown, B, perm, B.offs, order, s);
+    Bd = Bown;
+    b_kmajor = true;
+  }
+  // device table: one problem per output block, one segment per pair
+  std::vector<GroupedProblem> probs;
+  std::vector<GroupedSegment> segs;
+  for (size_t ob = 0; ob < C.nnzb(); ob++) {
+    const auto& prs = contrib[C.coords[ob]];
+    GroupedProblem pr{};
+    int64_t m = 1, n = 1;
+    for (size_t i : ua) m *= (int64_t)A.bsz[i][A.coords[prs[0].first][i]];
+    for (size_t j : ub) n *= (int64_t)B.bsz[j][B.coords[prs[0].second][j]];
+    pr.m = m;
+    pr.n = n;
+    pr.c_off = (int64_t)C.offs[ob];
+    pr.seg_begin = (int64_t)segs.size();
+    pr.seg_count = (int64_t)prs.size();
+    for (auto& p2 : prs) {
+      GroupedSegment sg{};
+      int64_t k = 1;
+      for (size_t i : pa) k *= (int64_t)A.bsz[i][A.coords[p2.first][i]];
+      sg.a_off = (int64_t)A.offs[p2.first];
+      sg.b_off = (int64_t)B.offs[p2.second];
+      sg.k = k;
+      sg.lda = a_kmajor ? k : m;
+      sg.ldb = b_kmajor ? k : n;
+      sg.scale_off = -1;
+      segs.push_back(sg);
+    }
+    probs.push_back(pr);
+  }
+  void* Cd = C.st->dev_overwrite();
+  void* Cu = permute_c ? dev_alloc(C.total() * es, dev) : Cd;
+  grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, nullptr, s);
+  if (permute_c) {
+    // contract_gemm returns each block in label-sorted order (same shape,
+    // checked above); the data is permuted block by block.
+    BlockSparseT tmp = C;
+    std::vector<size_t> order(C.nnzb());
+    for (size_t i = 0; i < order.size(); i++) order[i] = i;
+    // blocks of Cu are laid out in the unsorted axis order [A free..., B free...]
+    permute_blocks(C.dt, Cu, Cd, tmp, perm_c, C.offs, order, s);
+    dev_free(Cu, dev);
+  }
+  if (Aown) dev_free(Aown, dev);
+  if (Bown) dev_free(Bown, dev);
+  return C;
+}
+
+// permutedims_blocksparse (operations/blocksparse.rs:61-129)
+BlockSparseT bs_permutedims(const BlockSparseT& A, const std::vector<size_t>& perm) {
+  const size_t nd = A.ndim();
+  if (perm.size() != nd) throw Error(ErrKind::InvalidPermutation, "invalid permutation");
+  std::vector<char> seen(nd, 0);
+  for (size_t p : perm) {
+    if (p >= nd || seen[p]) throw Error(ErrKind::InvalidPermutation, "invalid permutation");
+    seen[p] = 1;
+  }
+  BlockSparseT C;
+  C.dt = A.dt;
+  for (size_t i = 0; i < nd; i++) C.bsz.push_back(A.bsz[perm[i]]);
+  std::vector<std::pair<std::vector<size_t>, size_t>> pc;
+  for (size_t b = 0; b < A.nnzb(); b++) {
+    std::vector<size_t> c(nd);
+    for (size_t i = 0; i < nd; i++) c[i] = A.coords[b][perm[i]];
+    pc.push_back({c, b});
+    if (A.block_elems(A.coords[b]) == 0) throw Error(ErrKind::Panic, "permutedims of a zero-size block");
+  }
+  std::sort(pc.begin(), pc.end());
+  std::vector<size_t> order;
+  for (auto& x : pc) {
+    C.coords.push_back(x.first);
+    order.push_back(x.second);
+  }
+  C.pack();
+  C.st = std::make_shared<Storage>(C.dt, C.total());
+  if (C.total() == 0) {
+    C.st->set_uniform(0.0, 0.0);
+    return C;
+  }
+  const void* Ad = A.st->dev_read();
+  void* Cd = C.st->dev_overwrite();
+  std::vector<size_t> dst_offs(C.offs.begin(), C.offs.end() - 1);
+  permute_blocks(A.dt, Ad, Cd, A, perm, dst_offs, order, ctx().compute);
+  return C;
+}
+
+static std::vector<BsBlockDesc> dense_tables(const BlockSparseT& A, std::vector<int64_t>* offs) {
+  std::vector<size_t> dshape(A.ndim());
+  for (size_t i = 0; i < A.ndim(); i++) dshape[i] = A.dense_extent(i);
+  std::vector<size_t> dst = col_major_strides(dshape);
+  std::vector<BsBlockDesc> tab;
+  offs->clear();
+  for (size_t b = 0; b < A.nnzb(); b++) {
+    if (A.block_elems(A.coords[b]) == 0) continue;
+    BsBlockDesc d{};
+    d.ndim = (int32_t)A.ndim();
+    d.dense_base = 0;
+    for (size_t i = 0; i < A.ndim(); i++) {
+      d.shape[i] = (int64_t)A.bsz[i][A.coords[b][i]];
+      d.dstride[i] = (int64_t)dst[i];
+      d.dense_base += (int64_t)(A.block_start(i, A.coords[b][i]) * dst[i]);
+    }
+    tab.push_back(d);
+    offs->push_back((int64_t)A.offs[b]);
+  }
+  return tab;
+}
+
+// BlockSparseTensor::to_dense (blocksparse_tensor.rs:290-324)
+Dense bs_to_dense(const BlockSparseT& A) {
+  std::vector<size_t> dshape(A.ndim());
+  for (size_t i = 0; i < A.ndim(); i++) dshape[i] = A.dense_extent(i);
+  Dense out = make_uniform(A.dt, dshape, 0.0, 0.0);
+  if (A.total() == 0) return out;
+  void* dd = const_cast<void*>(out.st->dev_read());  // materialise zeros on device
+  out.st->dev_overwrite();
+  std::vector<int64_t> offs;
+  std::vector<BsBlockDesc> tab = dense_tables(A, &offs);
+  bs_dense_map(A.dt, const_cast<void*>(A.st->dev_read()), dd, offs, tab, (int64_t)A.total(), true, ctx().compute);
+  return out;
+}
+
+// BlockSparseTensor::from_dense (blocksparse_tensor.rs:353-391)
+BlockSparseT bs_from_dense(const Dense& dense, const std::vector<std::vector<size_t>>& bsz,
+                           const std::vector<std::vector<size_t>>& coords) {
+  BlockSparseT A = make_bs(dense.dt, bsz, coords);
+  std::vector<size_t> dshape(A.ndim());
+  for (size_t i = 0; i < A.ndim(); i++) dshape[i] = A.dense_extent(i);
+  if (dshape != dense.shape) throw Error(ErrKind::ShapeMismatch, "dense shape does not match block dims");
+  if (A.total() == 0) return A;
+  void* p = A.st->dev_overwrite();
+  std::vector<int64_t> offs;
+  std::vector<BsBlockDesc> tab = dense_tables(A, &offs);
+  bs_dense_map(A.dt, p, const_cast<void*>(dense.st->dev_read()), offs, tab, (int64_t)A.total(), false,
+               ctx().compute);
+  return A;
+}
+
+static DiagBlockSparseT make_diag(DType dt, const std::vector<std::vector<size_t>>& bsz,
+                                  const std::vector<std::vector<size_t>>& coords) {
+  check_structure(bsz, coords);
+  DiagBlockSparseT S;
+  S.s.dt = dt;
+  S.s.bsz = bsz;
+  S.s.coords = coords;
+  // diagblocksparse.rs:218-230: offsets packed by diagonal length
+  S.s.offs.assign(coords.size() + 1, 0);
+  for (size_t b = 0; b < coords.size(); b++) S.s.offs[b + 1] = S.s.offs[b] + S.diag_size(coords[b]);
+  S.s.st = std::make_shared<Storage>(dt, S.s.total());
+  S.s.st->set_uniform(0.0, 0.0);
+  return S;
+}
+
+// DiagBlockSparseTensor::to_dense (diagblocksparse_tensor.rs:399-426)
+Dense diag_to_dense(const DiagBlockSparseT& S) {
+  const BlockSparseT& t = S.s;
+  std::vector<size_t> dshape(t.ndim());
+  for (size_t i = 0; i < t.ndim(); i++) dshape[i] = t.dense_extent(i);
+  Dense out = make_uniform(t.dt, dshape, 0.0, 0.0);
+  if (t.total() == 0) return out;
+  void* dd = const_cast<void*>(out.st->dev_read());
+  out.st->dev_overwrite();
+  std::vector<size_t> dst = col_major_strides(dshape);
+  int64_t step = 0;
+  for (size_t x : dst) step += (int64_t)x;
+  std::vector<BsBlockDesc> tab;
+  std::vector<int64_t> offs;
+  for (size_t b = 0; b < t.nnzb(); b++) {
+    if (S.diag_size(t.coords[b]) == 0) continue;
+    BsBlockDesc d{};
+    d.ndim = 1;
+    for (size_t i = 0; i < t.ndim(); i++) d.dense_base += (int64_t)(t.block_start(i, t.coords[b][i]) * dst[i]);
+    d.dstride[0] = step;
+    tab.push_back(d);
+    offs.push_back((int64_t)t.offs[b]);
+  }
+  diag_scatter(t.dt, t.st->dev_read(), dd, offs, tab, (int64_t)t.total(), ctx().compute);
+  return out;
+}
+
+// The diagonal tensor as a block-sparse tensor with dense diagonal blocks
+// (the same values as to_dense restricted to the stored blocks).
+BlockSparseT diag_to_blocksparse(const DiagBlockSparseT& S) {
+  const BlockSparseT& t = S.s;
+  BlockSparseT C = make_bs(t.dt, t.bsz, t.coords);
+  if (C.total() == 0) return C;
+  void* cd = const_cast<void*>(C.st->dev_read());  // zeros on device
+  C.st->dev_overwrite();
+  std::vector<BsBlockDesc> tab;
+  std::vector<int64_t> offs;
+  for (size_t b = 0; b < t.nnzb(); b++) {
+    size_t ds = S.diag_size(t.coords[b]);
+    if (ds == 0) continue;
+    std::vector<size_t> st = col_major_strides(C.block_shape(C.coords[b]));
+    BsBlockDesc d{};
+    d.ndim = 1;
+    d.dense_base = (int64_t)C.offs[b];
+    for (size_t x : st) d.dstride[0] += (int64_t)x;
+    tab.push_back(d);
+    offs.push_back((int64_t)t.offs[b]);
+  }
+  diag_scatter(t.dt, t.st->dev_read(), cd, offs, tab, (int64_t)t.total(), ctx().compute);
+  return C;
+}
+
+// A (block-sparse) x S (diag-block-sparse): the contraction of A with
+// diag_to_blocksparse(S) under contract_blocksparse semantics.  When S is
+// rank 2, contracted with A's last axis, its other axis kept, and every A
+// block meets at most one S block (and lands in its own output block), the
+// product is a diagonal scaling of A's last axis: one elementwise kernel
+// instead of a GEMM per block.  Otherwise the general block contraction runs.
+BlockSparseT bs_contract_diag(const BlockSparseT& A, const std::vector<int32_t>& la, const DiagBlockSparseT& S,
+                              const std::vector<int32_t>& ls) {
+  const BlockSparseT& t = S.s;
+  const size_t na = A.ndim();
+  bool fast = t.ndim() == 2 && na >= 1 && la.size() == na && ls.size() == 2 && A.dt == t.dt;
+  size_t js = 0, jo = 1;
+  if (fast) {
+    // exactly one pair: A's last axis with one S axis; S's other axis positive
+    int pairs = 0;
+    for (size_t i = 0; i < na; i++)
+      if (la[i] < 0 && (la[i] == ls[0] || la[i] == ls[1])) pairs++;
+    fast = pairs == 1 && la[na - 1] < 0 && (la[na - 1] == ls[0] || la[na - 1] == ls[1]);
+    if (fast) {
+      js = la[na - 1] == ls[0] ? 0 : 1;
+      jo = 1 - js;
+      fast = ls[jo] > 0 && ls[js] != ls[jo];
+      // output labels ascending (no contract_gemm re-sort)
+      int32_t prev = INT32_MIN;
+      for (size_t i = 0; i + 1 < na && fast; i++) {
+        if (la[i] <= 0) fast = false;  // all other A axes must be free positive axes
+        if (la[i] < prev) fast = false;
+        prev = la[i];
+      }
+      if (fast && ls[jo] < prev) fast = false;
+      if (fast && A.bsz[na - 1] != t.bsz[js]) fast = false;
+    }
+  }
+  std::map<size_t, size_t> srow;  // S coordinate on js -> S block
+  if (fast) {
+    for (size_t b = 0; b < t.nnzb(); b++) {
+      size_t key = t.coords[b][js];
+      if (srow.count(key)) fast = false;
+      srow[key] = b;
+    }
+  }
+  if (!fast) return bs_contract(A, la, diag_to_blocksparse(S), ls, 0, 1);
+  BlockSparseT C;
+  C.dt = A.dt;
+  for (size_t i = 0; i + 1 < na; i++) C.bsz.push_back(A.bsz[i]);
+  C.bsz.push_back(t.bsz[jo]);
+  std::map<std::vector<size_t>, std::pair<size_t, size_t>> outs;  // sorted: out coords -> (A block, S block)
+  for (size_t a = 0; a < A.nnzb(); a++) {
+    auto it = srow.find(A.coords[a][na - 1]);
+    if (it == srow.end()) continue;
+    std::vector<size_t> oc(A.coords[a].begin(), A.coords[a].end() - 1);
+    oc.push_back(t.coords[it->second][jo]);
+    if (outs.count(oc)) return bs_contract(A, la, diag_to_blocksparse(S), ls, 0, 1);
+    outs[oc] = {a, it->second};
+  }
+  for (auto& kv : outs) C.coords.push_back(kv.first);
+  C.pack();
+  C.st = std::make_shared<Storage>(C.dt, C.total());
+  if (C.total() == 0) {
+    C.st->set_uniform(0.0, 0.0);
+    return C;
+  }
+  std::vector<BsBlockDesc> tab;
+  std::vector<int64_t> offs;
+  size_t ob = 0;
+  for (auto& kv : outs) {
+    size_t a = kv.second.first, sb = kv.second.second;
+    std::vector<size_t> sh = C.block_shape(C.coords[ob]);
+    BsBlockDesc d{};
+    d.ndim = 3;
+    int64_t inner = 1;
+    for (size_t i = 0; i + 1 < sh.size(); i++) inner *= (int64_t)sh[i];
+    d.shape[0] = inner;
+    d.shape[1] = (int64_t)sh.back();
+    d.shape[2] = (int64_t)S.diag_size(t.coords[sb]);
+    d.dense_base = (int64_t)A.offs[a];
+    d.dstride[0] = (int64_t)t.offs[sb];
+    if (C.block_elems(C.coords[ob]) > 0) {
+      tab.push_back(d);
+      offs.push_back((int64_t)C.offs[ob]);
+    }
+    ob++;
+  }
+  void* cd = C.st->dev_overwrite();
+  bs_diag_scale(A.dt, A.st->dev_read(), t.st->dev_read(), cd, offs, tab, (int64_t)C.total(), ctx().compute);
+  return C;
+}
+
+}  // namespace ndt
+
+// =========================================================================
+// C ABI (additive: the reference's C ABI has no block-sparse symbols)
+// =========================================================================
+using namespace ndt;
+
+struct NdtBs {
+  BlockSparseT t;
+};
+struct NdtDiag {
+  DiagBlockSparseT t;
+};
+
+namespace {
+
+int map_err(const Error& e, int code) {
+  set_last_error(e.what());
+  switch (e.kind) {
+    case ErrKind::Panic:
+    case ErrKind::Cuda:
+      return NDT_INTERNAL_ERROR;
+    case ErrKind::InvalidArgument:
+      return NDT_INVALID_ARGUMENT;
+    case ErrKind::BlockNotFound:
+    case ErrKind::IndexOutOfBounds:
+      return NDT_INDEX_OUT_OF_BOUNDS;
+    default:
+      return code;
+  }
+}
+
+template <class F>
+void* guarded(int* status, int code, F&& f) {
+  if (!status) return nullptr;
+  try {
+    void* r = f();
+    *status = NDT_SUCCESS;
+    return r;
+  } catch (const Error& e) {
+    *status = map_err(e, code);
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    *status = NDT_INTERNAL_ERROR;
+  } catch (...) {
+    *status = NDT_INTERNAL_ERROR;
+  }
+  return nullptr;
+}
+
+template <class F>
+int guarded_int(int code, F&& f) {
+  try {
+    return f();
+  } catch (const Error& e) {
+    return map_err(e, code);
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return NDT_INTERNAL_ERROR;
+  } catch (...) {
+    return NDT_INTERNAL_ERROR;
+  }
+}
+
+void read_structure(size_t ndim, const size_t* nblocks, const size_t* block_sizes, size_t nnzb, const size_t* coords,
+                    std::vector<std::vector<size_t>>* bsz, std::vector<std::vector<size_t>>* cs) {
+  if ((ndim && (!nblocks || !block_sizes)) || (nnzb && ndim && !coords))
+    throw Error(ErrKind::InvalidArgument, "NULL structure array");
+  size_t k = 0;
+  for (size_t i = 0; i < ndim; i++) {
+    bsz->push_back(std::vector<size_t>(block_sizes + k, block_sizes + k + nblocks[i]));
+    k += nblocks[i];
+  }
+  for (size_t b = 0; b < nnzb; b++) cs->push_back(std::vector<size_t>(coords + b * ndim, coords + (b + 1) * ndim));
+}
+
+std::vector<int32_t> labels(const long* l, size_t n) {
+  std::vector<int32_t> v(n);
+  for (size_t i = 0; i < n; i++) v[i] = (int32_t)l[i];
+  return v;
+}
+
+void* bs_new(DType dt, size_t ndim, const size_t* nblocks, const size_t* block_sizes, size_t nnzb,
+             const size_t* coords, const double* data, size_t len, int* status) {
+  return guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {
+    std::vector<std::vector<size_t>> bsz, cs;
+    read_structure(ndim, nblocks, block_sizes, nnzb, coords, &bsz, &cs);
+    BlockSparseT t = make_bs(dt, bsz, cs);
+    if (data) {
+      if (len != t.total()) throw Error(ErrKind::ShapeMismatch, "data length != total block elements");
+      if (t.total()) {
+        Dense tmp = make_from_host(dt, data, len, {len});
+        t.st = tmp.st;
+      }
+    }
+    return new NdtBs{t};
+  });
+}
+
+int bs_insert(void* h, const size_t* coords, const double* data, size_t len) {
+  if (!h || !coords || !data) return NDT_INVALID_ARGUMENT;
+  return guarded_int(NDT_SHAPE_MISMATCH, [&]() {
+    BlockSparseT& t = ((NdtBs*)h)->t;
+    std::vector<size_t> c(coords, coords + t.ndim());
+    long b = t.find(c);
+    if (b < 0) return NDT_INDEX_OUT_OF_BOUNDS;  // TensorError::BlockNotFound
+    // insertblock: data shape must equal the block shape (blocksparse_tensor.rs:210-235)
+    if (len != t.block_elems(c)) return NDT_SHAPE_MISMATCH;
+    if (t.st.use_count() > 1) t.st = t.st->clone();
+    if (!device_available()) {  // host-only bookkeeping (no computation happens here)
+      char* h = (char*)t.st->host_write();
+      memcpy(h + t.offs[b] * esize(t.dt), data, len * esize(t.dt));
+      return NDT_SUCCESS;
+    }
+    void* p = const_cast<void*>(t.st->dev_read());
+    t.st->dev_overwrite();
+    NDT_CUDA(cudaMemcpyAsync((char*)p + t.offs[b] * esize(t.dt), data, len * esize(t.dt), cudaMemcpyHostToDevice,
+                             ctx().compute));
+    NDT_CUDA(cudaStreamSynchronize(ctx().compute));
+    return NDT_SUCCESS;
+  });
+}
+
+int bs_get(const void* h, const size_t* coords, double* out, size_t len) {
+  if (!h || !coords || !out) return NDT_INVALID_ARGUMENT;
+  return guarded_int(NDT_SHAPE_MISMATCH, [&]() {
+    const BlockSparseT& t = ((const NdtBs*)h)->t;
+    std::vector<size_t> c(coords, coords + t.ndim());
+    long b = t.find(c);
+    if (b < 0) return NDT_INDEX_OUT_OF_BOUNDS;
+    if (len < t.block_elems(c)) return NDT_SHAPE_MISMATCH;
+    const double* host = (const double*)t.st->host_read();
+    memcpy(out, host + t.offs[b] * (esize(t.dt) / 8), t.block_elems(c) * esize(t.dt));
+    return NDT_SUCCESS;
+  });
+}
+
+int bs_structure(const void* h, size_t* nblocks, size_t* block_sizes, size_t* coords, size_t* offsets) {
+  if (!h) return NDT_INVALID_ARGUMENT;
+  const BlockSparseT& t = ((const NdtBs*)h)->t;
+  size_t k = 0;
+  for (size_t i = 0; i < t.ndim(); i++) {
+    if (nblocks) nblocks[i] = t.bsz[i].size();
+    for (size_t x : t.bsz[i]) {
+      if (block_sizes) block_sizes[k] = x;
+      k++;
+    }
+  }
+  for (size_t b = 0; b < t.nnzb(); b++) {
+    for (size_t i = 0; i < t.ndim(); i++)
+      if (coords) coords[b * t.ndim() + i] = t.coords[b][i];
+    if (offsets) offsets[b] = t.offs[b];
+  }
+  return NDT_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+#define NDT_BS_COMMON(T, DT)                                                                                           \
+  T* ndt_blocksparse_##DT##_zeros(size_t ndim, const size_t* nblocks, const size_t* block_sizes, size_t nnzb,         \
+                                  const size_t* coords, int* status) {                                               \
+    return (T*)bs_new(DTYPE_##DT, ndim, nblocks, block_sizes, nnzb, coords, nullptr, 0, status);                     \
+  }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes, size_t nnzb,    \
+                                      const size_t* coords, const double* data, size_t len, int* status) {           \
+    if (!data) {                                                                                                     \
+      if (status) *status = NDT_INVALID_ARGUMENT;                                                                    \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+    return (T*)bs_new(DTYPE_##DT, ndim, nblocks, block_sizes, nnzb, coords, data, len, status);                      \
+  }                                                                                                                  \
+  void ndt_blocksparse_##DT##_release(T* t) { delete (NdtBs*)t; }                                                    \
+  size_t ndt_blocksparse_##DT##_ndim(const T* t) { return t ? ((const NdtBs*)t)->t.ndim() : 0; }                     \
+  size_t ndt_blocksparse_##DT##_nnzblocks(const T* t) { return t ? ((const NdtBs*)t)->t.nnzb() : 0; }                \
+  size_t ndt_blocksparse_##DT##_nnz(const T* t) { return t ? ((const NdtBs*)t)->t.total() : 0; }                     \
+  size_t ndt_blocksparse_##DT##_nblocks_total(const T* t) {                                                          \
+    if (!t) return 0;                                                                                                \
+    size_t s = 0;                                                                                                    \
+    for (auto& v : ((const NdtBs*)t)->t.bsz) s += v.size();                                                          \
+    return s;                                                                                                        \
+  }                                                                                                                  \
+  int ndt_blocksparse_##DT##_structure(const T* t, size_t* nblocks, size_t* block_sizes, size_t* coords,             \
+                                       size_t* offsets) {                                                            \
+    return bs_structure(t, nblocks, block_sizes, coords, offsets);                                                   \
+  }                                                                                                                  \
+  int ndt_blocksparse_##DT##_insert_block(T* t, const size_t* coords, const double* data, size_t len) {              \
+    return bs_insert(t, coords, data, len);                                                                          \
+  }                                                                                                                  \
+  int ndt_blocksparse_##DT##_get_block(const T* t, const size_t* coords, double* out, size_t len) {                  \
+    return bs_get(t, coords, out, len);                                                                              \
+  }                                                                                                                  \
+  const double* ndt_blocksparse_##DT##_data(const T* t) {                                                            \
+    if (!t) return nullptr;                                                                                          \
+    try {                                                                                                            \
+      return (const double*)((const NdtBs*)t)->t.st->host_read();                                                    \
+    } catch (const std::exception& e) {                                                                              \
+      set_last_error(e.what());                                                                                      \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+  }                                                                                                                  \
+  const double* ndt_blocksparse_##DT##_device_ptr(const T* t) {                                                      \
+    if (!t) return nullptr;                                                                                          \
+    try {                                                                                                            \
+      return (const double*)((const NdtBs*)t)->t.st->dev_read();                                                     \
+    } catch (const std::exception& e) {                                                                              \
+      set_last_error(e.what());                                                                                      \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+  }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_contract(const T* a, const long* la, size_t na, const T* b, const long* lb, size_t nb,   \
+                                     int* status) {                                                                  \
+    if (!status) return nullptr;                                                                                     \
+    if (!a || !b || (!la && na) || (!lb && nb)) {                                                                    \
+      *status = NDT_INVALID_ARGUMENT;                                                                                \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
+      return new NdtBs{bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), 0, 1)}; \
+    });                                                                                                              \
+  }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_contract_shard(const T* a, const long* la, size_t na, const T* b, const long* lb,        \
+                                           size_t nb, int rank, int nranks, int* status) {                           \
+    if (!status) return nullptr;                                                                                     \
+    if (!a || !b || (!la && na) || (!lb && nb) || nranks < 1 || rank < 0 || rank >= nranks) {                        \
+      *status = NDT_INVALID_ARGUMENT;                                                                                \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
+      return new NdtBs{                                                                                              \
+          bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), rank, nranks)};    \
+    });                                                                                                              \
+  }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_permutedims(const T* a, const size_t* perm, size_t nperm, int* status) {                 \
+    if (!status) return nullptr;                                                                                     \
+    if (!a || (!perm && nperm)) {                                                                                    \
+      *status = NDT_INVALID_ARGUMENT;                                                                                \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+    return (T*)guarded(status, NDT_INVALID_PERMUTATION, [&]() -> void* {                                             \
+      return new NdtBs{bs_permutedims(((const NdtBs*)a)->t, std::vector<size_t>(perm, perm + nperm))};               \
+    });                                                                                                              \
+  }
+
+#define DTYPE_f64 DType::F64
+#define DTYPE_c64 DType::C128
+NDT_BS_COMMON(ndt_blocksparse_f64, f64)
+NDT_BS_COMMON(ndt_blocksparse_c64, c64)
+
+// Host-only planning of the sharded contraction: output blocks and real
+// flops per rank (no device work).
+#define NDT_BS_PLAN(T, DT)                                                                                          \
+  int ndt_blocksparse_##DT##_shard_plan(const T* a, const long* la, size_t na, const T* b, const long* lb,         \
+                                        size_t nb, int nranks, size_t* blocks_per_rank, double* flops_per_rank) {   \
+    if (!a || !b || (!la && na) || (!lb && nb) || nranks < 1) return NDT_INVALID_ARGUMENT;                         \
+    return guarded_int(NDT_SHAPE_MISMATCH, [&]() {                                                                 \
+      ShardPlan p;                                                                                                 \
+      bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), 0, nranks, &p);      \
+      for (int r = 0; r < nranks; r++) {                                                                           \
+        if (blocks_per_rank) blocks_per_rank[r] = p.blocks[r];                                                     \
+        if (flops_per_rank) flops_per_rank[r] = p.flops[r];                                                        \
+      }                                                                                                            \
+      return NDT_SUCCESS;                                                                                          \
+    });                                                                                                            \
+  }
+NDT_BS_PLAN(ndt_blocksparse_f64, f64)
+NDT_BS_PLAN(ndt_blocksparse_c64, c64)
+
+ndt_tensor_f64* ndt_blocksparse_f64_to_dense(const ndt_blocksparse_f64* a, int* status) {
+  if (status && !a) {
+    *status = NDT_INVALID_ARGUMENT;
+    return nullptr;
+  }
+  return (ndt_tensor_f64*)guarded(status, NDT_SHAPE_MISMATCH,
+                                  [&]() -> void* { return new NdtHandle{bs_to_dense(((const NdtBs*)a)->t)}; });
+}
+ndt_tensor_c64* ndt_blocksparse_c64_to_dense(const ndt_blocksparse_c64* a, int* status) {
+  if (status && !a) {
+    *status = NDT_INVALID_ARGUMENT;
+    return nullptr;
+  }
+  return (ndt_tensor_c64*)guarded(status, NDT_SHAPE_MISMATCH,
+                                  [&]() -> void* { return new NdtHandle{bs_to_dense(((const NdtBs*)a)->t)}; });
+}
+
+#define NDT_BS_FROM_DENSE(T, TD, DT)                                                                                  \
+  T* ndt_blocksparse_##DT##_from_dense(const TD* dense, size_t ndim, const size_t* nblocks, const size_t* block_sizes, \
+                                       size_t nnzb, const size_t* coords, int* status) {                              \
+    if (status && !dense) {                                                                                           \
+      *status = NDT_INVALID_ARGUMENT;                                                                                 \
+      return nullptr;                                                                                                 \
+    }                                                                                                                 \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                   \
+      std::vector<std::vector<size_t>> bsz, cs;                                                                       \
+      read_structure(ndim, nblocks, block_sizes, nnzb, coords, &bsz, &cs);                                            \
+      const Dense& d = ((const NdtHandle*)dense)->t;                                                             \
+      if (d.dt != DTYPE_##DT) throw Error(ErrKind::InvalidArgument, "element type mismatch");                         \
+      return new NdtBs{bs_from_dense(d, bsz, cs)};                                                                    \
+    });                                                                                                               \
+  }
+NDT_BS_FROM_DENSE(ndt_blocksparse_f64, ndt_tensor_f64, f64)
+NDT_BS_FROM_DENSE(ndt_blocksparse_c64, ndt_tensor_c64, c64)
+
+// ---- diag-block-sparse
+#define NDT_DIAG(T, TD, TB, DT)                                                                                         \
+  T* ndt_diagblocksparse_##DT##_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes, size_t nnzb,  \
+                                          const size_t* coords, const double* diag, size_t len, int* status) {          \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                     \
+      if (!diag) throw Error(ErrKind::InvalidArgument, "NULL data");                                                    \
+      std::vector<std::vector<size_t>> bsz, cs;                                                                         \
+      read_structure(ndim, nblocks, block_sizes, nnzb, coords, &bsz, &cs);                                              \
+      DiagBlockSparseT S = make_diag(DTYPE_##DT, bsz, cs);                                                              \
+      if (len != S.s.total()) throw Error(ErrKind::ShapeMismatch, "diag length != total diagonal elements");            \
+      if (len) S.s.st = make_from_host(DTYPE_##DT, diag, len, {len}).st;                                                \
+      return new NdtDiag{S};                                                                                            \
+    });                                                                                                                 \
+  }                                                                                                                     \
+  void ndt_diagblocksparse_##DT##_release(T* t) { delete (NdtDiag*)t; }                                                 \
+  size_t ndt_diagblocksparse_##DT##_nnz(const T* t) { return t ? ((const NdtDiag*)t)->t.s.total() : 0; }                \
+  TD* ndt_diagblocksparse_##DT##_to_dense(const T* s, int* status) {                                                    \
+    if (status && !s) {                                                                                                 \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TD*)guarded(status, NDT_SHAPE_MISMATCH,                                                                     \
+                        [&]() -> void* { return new NdtHandle{diag_to_dense(((const NdtDiag*)s)->t)}; });          \
+  }                                                                                                                     \
+  TB* ndt_diagblocksparse_##DT##_to_blocksparse(const T* s, int* status) {                                              \
+    if (status && !s) {                                                                                                 \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH,                                                                     \
+                        [&]() -> void* { return new NdtBs{diag_to_blocksparse(((const NdtDiag*)s)->t)}; });             \
+  }                                                                                                                     \
+  TB* ndt_blocksparse_##DT##_contract_diag(const TB* a, const long* la, size_t na, const T* s, const long* ls,          \
+                                           size_t ns, int* status) {                                                    \
+    if (!status) return nullptr;                                                                                        \
+    if (!a || !s || (!la && na) || (!ls && ns)) {                                                                       \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                    \
+      return new NdtBs{bs_contract_diag(((const NdtBs*)a)->t, labels(la, na), ((const NdtDiag*)s)->t, labels(ls, ns))}; \
+    });                                                                                                                 \
+  }
+NDT_DIAG(ndt_diagblocksparse_f64, ndt_tensor_f64, ndt_blocksparse_f64, f64)
+NDT_DIAG(ndt_diagblocksparse_c64, ndt_tensor_c64, ndt_blocksparse_c64, c64)
+
+}  // extern "C"

@@ -1,0 +1,167 @@
+// Device kernels for block-sparse storage.
+//
+//   bs_dense_map      packed block data <-> dense tensor (to_dense / from_dense,
+//                     blocksparse_tensor.rs:290-391): one thread per packed
+//                     element, the block found by binary search over the
+//                     packed offsets, the dense offset from the block's start
+//                     and the dense strides.
+//   diag_scatter      diagonal values -> dense tensor or dense diagonal blocks
+//                     (diagblocksparse_tensor.rs:399-426).
+//   bs_diag_scale     out block = A block with its last axis scaled by the
+//                     diagonal of the matching diag block (the fused
+//                     block-sparse x diag-block-sparse contraction).
+#include <algorithm>
+#include <cstring>
+
+#include "ndt_internal.h"
+
+namespace ndt {
+
+namespace {
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ int find_block(const int64_t* offs, int nblocks, int64_t e) {
+  int lo = 0, hi = nblocks - 1;  // offs[b] <= e < offs[b+1]
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (offs[mid] <= e)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+template <typename T>
+__global__ void dense_map_kernel(T* packed, T* dense, const int64_t* __restrict__ offs,
+                                 const BsBlockDesc* __restrict__ blocks, int nblocks, int64_t total, int to_dense) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = find_block(offs, nblocks, e);
+    const BsBlockDesc& d = blocks[b];
+    int64_t r = e - offs[b], off = d.dense_base;
+    for (int k = 0; k < d.ndim; k++) {
+      int64_t i = r % d.shape[k];
+      r /= d.shape[k];
+      off += i * d.dstride[k];
+    }
+    if (to_dense)
+      dense[off] = packed[e];
+    else
+      packed[e] = dense[off];
+  }
+}
+
+template <typename T>
+__global__ void diag_scatter_kernel(const T* __restrict__ diag, T* out, const int64_t* __restrict__ offs,
+                                    const BsBlockDesc* __restrict__ blocks, int nblocks, int64_t total) {
+  // element i of diagonal block b goes to out[dense_base + i * dstride[0]]
+  // (dstride[0] holds the sum of the strides along every axis)
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = find_block(offs, nblocks, e);
+    const BsBlockDesc& d = blocks[b];
+    out[d.dense_base + (e - offs[b]) * d.dstride[0]] = diag[e];
+  }
+}
+
+__device__ __forceinline__ double mulc(double a, double s) { return a * s; }
+__device__ __forceinline__ double2 mulc(double2 a, double2 s) {
+  return make_double2(a.x * s.x - a.y * s.y, a.x * s.y + a.y * s.x);
+}
+
+template <typename T>
+__global__ void diag_scale_kernel(const T* __restrict__ a, const T* __restrict__ s, T* out,
+                                  const int64_t* __restrict__ offs, const BsBlockDesc* __restrict__ blocks,
+                                  int nblocks, int64_t total) {
+  // out[offs[b] + e'] = a[src_off + e'] * s[diag_off + e' / inner] for e' < inner * nlast_valid,
+  // zero beyond; dense_base = source offset, dstride[0] = diag offset,
+  // shape[0] = inner (product of all but the last extent), shape[1] = last
+  // extent of the output block, shape[2] = diagonal length.
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
+    const int b = find_block(offs, nblocks, e);
+    const BsBlockDesc& d = blocks[b];
+    const int64_t r = e - offs[b];
+    const int64_t j = r / d.shape[0];
+    T v;
+    if (j < d.shape[2]) {
+      v = mulc(a[d.dense_base + r], s[d.dstride[0] + j]);
+    } else {
+      v = T{};
+    }
+    out[e] = v;
+  }
+}
+
+int grid_of(int64_t n) {
+  const DeviceCtx& c = ctx();
+  int64_t g = (n + kThreads - 1) / kThreads;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(g, (int64_t)c.sm_count * 8));
+}
+
+struct Tables {
+  int64_t* offs;
+  BsBlockDesc* blocks;
+  void* mem;
+};
+
+Tables upload(const std::vector<int64_t>& offs, const std::vector<BsBlockDesc>& blocks, cudaStream_t s) {
+  size_t b1 = offs.size() * sizeof(int64_t);
+  size_t o2 = (b1 + 255) / 256 * 256;
+  size_t total = o2 + blocks.size() * sizeof(BsBlockDesc);
+  std::vector<char> h(total);
+  memcpy(h.data(), offs.data(), b1);
+  memcpy(h.data() + o2, blocks.data(), blocks.size() * sizeof(BsBlockDesc));
+  void* d = nullptr;
+  NDT_CUDA(cudaMallocAsync(&d, total ? total : 16, s));
+  NDT_CUDA(cudaMemcpyAsync(d, h.data(), total, cudaMemcpyHostToDevice, s));
+  return Tables{(int64_t*)d, (BsBlockDesc*)((char*)d + o2), d};
+}
+}  // namespace
+
+void bs_dense_map(DType dt, void* packed, void* dense, const std::vector<int64_t>& offs,
+                  const std::vector<BsBlockDesc>& blocks, int64_t total, bool to_dense, cudaStream_t s) {
+  if (total <= 0 || blocks.empty()) return;
+  Tables t = upload(offs, blocks, s);
+  if (dt == DType::F64)
+    dense_map_kernel<double><<<grid_of(total), kThreads, 0, s>>>((double*)packed, (double*)dense, t.offs, t.blocks,
+                                                                 (int)blocks.size(), total, to_dense ? 1 : 0);
+  else
+    dense_map_kernel<double2><<<grid_of(total), kThreads, 0, s>>>((double2*)packed, (double2*)dense, t.offs,
+                                                                  t.blocks, (int)blocks.size(), total, to_dense ? 1 : 0);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+  NDT_CUDA(cudaFreeAsync(t.mem, s));
+}
+
+void diag_scatter(DType dt, const void* diag, void* out, const std::vector<int64_t>& offs,
+                  const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s) {
+  if (total <= 0 || blocks.empty()) return;
+  Tables t = upload(offs, blocks, s);
+  if (dt == DType::F64)
+    diag_scatter_kernel<double><<<grid_of(total), kThreads, 0, s>>>((const double*)diag, (double*)out, t.offs,
+                                                                    t.blocks, (int)blocks.size(), total);
+  else
+    diag_scatter_kernel<double2><<<grid_of(total), kThreads, 0, s>>>((const double2*)diag, (double2*)out, t.offs,
+                                                                     t.blocks, (int)blocks.size(), total);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+  NDT_CUDA(cudaFreeAsync(t.mem, s));
+}
+
+void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const std::vector<int64_t>& offs,
+                   const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s) {
+  if (total <= 0 || blocks.empty()) return;
+  Tables t = upload(offs, blocks, s);
+  if (dt == DType::F64)
+    diag_scale_kernel<double><<<grid_of(total), kThreads, 0, s>>>((const double*)a, (const double*)sdiag,
+                                                                  (double*)out, t.offs, t.blocks,
+                                                                  (int)blocks.size(), total);
+  else
+    diag_scale_kernel<double2><<<grid_of(total), kThreads, 0, s>>>((const double2*)a, (const double2*)sdiag,
+                                                                   (double2*)out, t.offs, t.blocks,
+                                                                   (int)blocks.size(), total);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+  NDT_CUDA(cudaFreeAsync(t.mem, s));
+}
+
+}  // namespace ndt

@@ -16,10 +16,6 @@
 
 using namespace ndt;
 
-struct NdtHandle {
-  Dense t;
-};
-
 namespace {
 
 NdtHandle* H(const void* p) { return (NdtHandle*)p; }

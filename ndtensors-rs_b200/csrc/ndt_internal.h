@@ -186,6 +186,23 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
                   const void* kscale, cudaStream_t s);
 
+// Block-sparse device helpers (blocksparse_kernels.cu).  A block table entry
+// describes one block: its extents, and for the dense side its start offset
+// and the dense strides (meaning of the fields per kernel is documented there).
+constexpr int kBsMaxRank = 16;
+struct BsBlockDesc {
+  int32_t ndim;
+  int64_t shape[kBsMaxRank];
+  int64_t dstride[kBsMaxRank];
+  int64_t dense_base;
+};
+void bs_dense_map(DType dt, void* packed, void* dense, const std::vector<int64_t>& offs,
+                  const std::vector<BsBlockDesc>& blocks, int64_t total, bool to_dense, cudaStream_t s);
+void diag_scatter(DType dt, const void* diag, void* out, const std::vector<int64_t>& offs,
+                  const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s);
+void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const std::vector<int64_t>& offs,
+                   const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s);
+
 // Elementwise helpers
 void fill_device(DType dt, void* p, size_t n, double re, double im, cudaStream_t s);
 void add_device(DType dt, const void* a, const void* b, void* c, size_t n, cudaStream_t s);
@@ -200,3 +217,8 @@ void contract_vjp(const Dense& a, const std::vector<int32_t>& la, const Dense& b
 Dense add(const Dense& a, const Dense& b);  // apply_binary(+) semantics
 
 }  // namespace ndt
+
+// The object behind an ndt_tensor_f64* / ndt_tensor_c64* handle.
+struct NdtHandle {
+  ndt::Dense t;
+};

@@ -6,6 +6,7 @@ package binds its C ABI with ctypes and mirrors the reference's Python API
 block-sparse tensors.
 """
 
+from . import blocksparse
 from ._lib import get_lib, last_error, lib_path
 from .ops import contract, contract_gemm, contract_jvp, contract_vjp
 from .tensor import NDTensorsError, StatusCode, TensorC64, TensorF64, check_status

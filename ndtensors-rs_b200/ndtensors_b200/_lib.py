@@ -93,6 +93,44 @@ SIGNATURES = [
         [ctypes.c_int, ctypes.c_long, ctypes.c_long, ctypes.c_long, vp, ctypes.c_long, ctypes.c_int, vp,
          ctypes.c_long, ctypes.c_int, vp, ctypes.c_long, ctypes.c_int, vp],
     ),
+    *[
+        sig
+        for dt in ("f64", "c64")
+        for sig in [
+            (f"ndt_blocksparse_{dt}_zeros", vp, [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_int_p]),
+            (f"ndt_blocksparse_{dt}_from_data", vp,
+             [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_double_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_blocksparse_{dt}_release", None, [vp]),
+            (f"ndt_blocksparse_{dt}_ndim", ctypes.c_size_t, [vp]),
+            (f"ndt_blocksparse_{dt}_nnzblocks", ctypes.c_size_t, [vp]),
+            (f"ndt_blocksparse_{dt}_nnz", ctypes.c_size_t, [vp]),
+            (f"ndt_blocksparse_{dt}_nblocks_total", ctypes.c_size_t, [vp]),
+            (f"ndt_blocksparse_{dt}_structure", ctypes.c_int, [vp, c_size_p, c_size_p, c_size_p, c_size_p]),
+            (f"ndt_blocksparse_{dt}_insert_block", ctypes.c_int, [vp, c_size_p, c_double_p, ctypes.c_size_t]),
+            (f"ndt_blocksparse_{dt}_get_block", ctypes.c_int, [vp, c_size_p, c_double_p, ctypes.c_size_t]),
+            (f"ndt_blocksparse_{dt}_data", c_double_p, [vp]),
+            (f"ndt_blocksparse_{dt}_device_ptr", vp, [vp]),
+            (f"ndt_blocksparse_{dt}_contract", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_shard", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, c_int_p]),
+            (f"ndt_blocksparse_{dt}_shard_plan", ctypes.c_int,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, ctypes.c_int, c_size_p,
+              ctypes.POINTER(ctypes.c_double)]),
+            (f"ndt_blocksparse_{dt}_permutedims", vp, [vp, c_size_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_blocksparse_{dt}_to_dense", vp, [vp, c_int_p]),
+            (f"ndt_blocksparse_{dt}_from_dense", vp,
+             [vp, ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_int_p]),
+            (f"ndt_diagblocksparse_{dt}_from_data", vp,
+             [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_double_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_diagblocksparse_{dt}_release", None, [vp]),
+            (f"ndt_diagblocksparse_{dt}_nnz", ctypes.c_size_t, [vp]),
+            (f"ndt_diagblocksparse_{dt}_to_dense", vp, [vp, c_int_p]),
+            (f"ndt_diagblocksparse_{dt}_to_blocksparse", vp, [vp, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_diag", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
+        ]
+    ],
     (
         "ndt_b200_contract_f64_noalloc",
         ctypes.c_int,

@@ -1,0 +1,116 @@
+"""Block-sparse host logic that needs no GPU: structure bookkeeping, error
+codes, the FLOP-balanced shard plan, and the shard gather over
+torch.distributed (gloo, world size 2)."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from workloads import cfg4_tensors, flops_blocksparse
+
+
+def test_structure_queries(ndt):
+    bs = ndt.blocksparse
+    t = bs.BlockSparseF64.from_blocks([[2, 3], [4, 5]], [(1, 1), (0, 0)], np.arange(15 + 8, dtype=float))
+    assert t.ndim == 2 and t.nnzblocks == 2 and t.nnz == 23
+    assert t.block_sizes == [[2, 3], [4, 5]]
+    assert t.coords == [(1, 1), (0, 0)]  # storage order kept (BlockOffsets::from_blocks)
+    assert t.dense_shape == (5, 9)
+    np.testing.assert_array_equal(t.block((0, 0)), np.arange(15, 23, dtype=float).reshape((2, 4), order="F"))
+    t.insert_block((0, 0), np.ones((2, 4)))
+    np.testing.assert_array_equal(t.block((0, 0)), np.ones((2, 4)))
+    with pytest.raises(ValueError):
+        t.insert_block((0, 0), np.ones((3, 4)))  # wrong block shape (blocksparse_tensor.rs:218-223)
+    with pytest.raises(KeyError):
+        t.block((0, 1))
+
+
+def test_structure_errors(ndt):
+    bs = ndt.blocksparse
+    with pytest.raises(ndt.NDTensorsError):
+        bs.BlockSparseF64.zeros([[2, 3]], [(2,)])  # coordinate out of range
+    with pytest.raises(ndt.NDTensorsError):
+        bs.BlockSparseF64.zeros([[2, 3]], [(0,), (0,)])  # duplicate block
+    with pytest.raises(ValueError):
+        bs.BlockSparseF64.from_blocks([[2, 3]], [(0,)], np.zeros(3))  # length != 2
+
+
+def test_shard_plan_is_flop_balanced(ndt):
+    (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
+    bs = ndt.blocksparse
+    A = bs.BlockSparseF64.from_blocks(sa, ca, a)
+    B = bs.BlockSparseF64.from_blocks(sb, cb, b)
+    total = flops_blocksparse((sa, ca, a), la, (sb, cb, b), lb, False)
+    for n in (1, 2, 4, 8):
+        blocks, flops = bs.shard_plan(A, la, B, lb, n)
+        assert sum(blocks) == 489  # every output block in exactly one shard
+        assert abs(sum(flops) - total) <= 1e-9 * total
+        if n > 1:
+            # contiguous cuts never split a block; the largest output block
+            # bounds the imbalance
+            assert max(flops) <= total / n + max_block_flops((sa, ca), la, (sb, cb), lb) + 1
+
+
+def max_block_flops(A, la, B, lb):
+    sa, ca = A
+    sb, cb = B
+    per = {}
+    for c in ca:
+        for d in cb:
+            if c[2] == d[0] and c[3] == d[1]:
+                key = (c[0], c[1], d[2], d[3])
+                m = sa[0][c[0]] * sa[1][c[1]]
+                k = sa[2][c[2]] * sa[3][c[3]]
+                n = sb[2][d[2]] * sb[3][d[3]]
+                per[key] = per.get(key, 0) + 2.0 * m * n * k
+    return max(per.values())
+
+
+def _gather_worker(rank, world, port, q):
+    import sys
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "ndtensors-rs_b200"))
+    import ndtensors_b200 as ndt
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        sizes = [[2, 3, 1], [4, 1]]
+        all_coords = [(0, 0), (0, 1), (1, 0), (2, 1)]
+        lens = [8, 2, 12, 1]
+        offs = np.cumsum([0] + lens)
+        data = np.arange(offs[-1], dtype=float) * 1.5
+        lo, hi = (0, 2) if rank == 0 else (2, 4)  # contiguous shards of the sorted block list
+        shard = ndt.blocksparse.BlockSparseF64.from_blocks(sizes, all_coords[lo:hi], data[offs[lo]:offs[hi]])
+        full = ndt.blocksparse.allgather(shard)
+        ok = full.coords == all_coords and np.array_equal(full.to_numpy_data(), data)
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allgather_shards_gloo():
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=120) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+    assert sorted(res) == [(0, True), (1, True)]

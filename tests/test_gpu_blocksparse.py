@@ -1,0 +1,212 @@
+"""Block-sparse contraction on the GPU (one grouped DMMA launch) vs the
+oracle's restatement of contract_blocksparse (contract/blocksparse.rs:87-275).
+
+Block structure (output coordinates, order, block sizes, packed offsets) must
+match exactly; values within relative Frobenius error 1e-12."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from workloads import cfg4_tensors, cfg5_tensors
+
+pytestmark = pytest.mark.gpu
+RTOL = 1e-12
+
+
+def rel_fro(x, y):
+    x, y = np.asarray(x).ravel(), np.asarray(y).ravel()
+    n = np.linalg.norm(y)
+    return np.linalg.norm(x - y) / n if n > 0 else np.linalg.norm(x - y)
+
+
+def _cls(gpu, cplx):
+    return gpu.blocksparse.BlockSparseC64 if cplx else gpu.blocksparse.BlockSparseF64
+
+
+def _check(gpu, oracle, A, la, B, lb):
+    cplx = np.iscomplexobj(A[2])
+    cls = _cls(gpu, cplx)
+    got = gpu.blocksparse.contract(cls.from_blocks(*A), la, cls.from_blocks(*B), lb)
+    st, ref = oracle.bs_contract(oracle.BlockSparse(*A), la, oracle.BlockSparse(*B), lb)
+    assert st == 0
+    assert got.block_sizes == ref.block_sizes
+    assert got.coords == ref.coords  # sorted output blocks, packed offsets
+    assert rel_fro(got.to_numpy_data(), ref.data) <= RTOL
+    return got, ref
+
+
+def random_bs(rng, sizes, density, cplx):
+    coords = []
+    import itertools
+
+    for c in itertools.product(*[range(len(s)) for s in sizes]):
+        if rng.random() < density:
+            coords.append(c)
+    rng.shuffle(coords)  # arbitrary storage order
+    n = sum(int(np.prod([sizes[a][x] for a, x in enumerate(c)])) for c in coords)
+    data = rng.standard_normal(n) + (1j * rng.standard_normal(n) if cplx else 0)
+    return sizes, [tuple(c) for c in coords], data
+
+
+PATTERNS = [
+    # (sizes_a, la, sizes_b, lb)
+    ([[3, 5], [4, 2, 6]], [1, -1], [[4, 2, 6], [7, 1]], [-1, 2]),  # matmul, in place
+    ([[4, 2, 6], [3, 5]], [-1, 1], [[4, 2, 6], [7, 1]], [-1, 2]),  # A K-major
+    ([[3, 5], [4, 2, 6]], [1, -1], [[7, 1], [4, 2, 6]], [2, -1]),  # B MN-major
+    ([[2, 3], [3, 1], [2, 2]], [1, -1, -2], [[2, 2], [3, 1], [4, 1]], [-2, -1, 2]),  # permuted -> block packing
+    ([[2, 3], [3, 1]], [-1, -2], [[2, 3], [3, 1]], [-1, -2]),  # full contraction -> scalar block
+    ([[2, 3]], [1], [[4, 1]], [2]),  # outer product of block vectors
+    ([[3, 2], [2, 4], [5]], [1, -1, 2], [[2, 4], [3, 3]], [-1, 3]),  # middle contracted axis
+]
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+@pytest.mark.parametrize("sa,la,sb,lb", PATTERNS)
+def test_blocksparse_contract_matches_oracle(gpu, oracle, sa, la, sb, lb, cplx):
+    rng = np.random.default_rng(abs(hash((str(sa), str(la), str(sb), cplx))) % (2**32))
+    A = random_bs(rng, sa, 0.7, cplx)
+    B = random_bs(rng, sb, 0.7, cplx)
+    _check(gpu, oracle, A, la, B, lb)
+
+
+def test_blocksparse_unsorted_output_labels(gpu, oracle):
+    """Output labels not ascending: the reference stores contract_gemm's
+    label-sorted block data under the unsorted block coordinates when the
+    block shapes agree (square blocks here), and fails otherwise."""
+    rng = np.random.default_rng(77)
+    A = random_bs(rng, [[3, 3], [4, 2]], 1.0, False)  # every output block is 3 x 3
+    B = random_bs(rng, [[4, 2], [3, 3]], 1.0, False)
+    _check(gpu, oracle, A, [2, -1], B, [-1, 1])
+    A2 = random_bs(rng, [[3, 2], [4, 2]], 1.0, False)
+    B2 = random_bs(rng, [[4, 2], [5, 1]], 1.0, False)
+    st, _ = oracle.bs_contract(oracle.BlockSparse(*A2), [2, -1], oracle.BlockSparse(*B2), [-1, 1])
+    assert st == oracle.SHAPE_MISMATCH
+    with pytest.raises(ValueError):
+        gpu.blocksparse.contract(gpu.blocksparse.BlockSparseF64.from_blocks(*A2), [2, -1],
+                                 gpu.blocksparse.BlockSparseF64.from_blocks(*B2), [-1, 1])
+
+
+def test_blocksparse_no_matching_pairs_and_empty(gpu, oracle):
+    A = ([[2, 3], [4, 5]], [(0, 0)], np.ones(8))
+    B = ([[4, 5], [2, 2]], [(1, 0)], np.ones(10))
+    got, ref = _check(gpu, oracle, A, [1, -1], B, [-1, 2])
+    assert got.nnzblocks == 0
+    E = ([[2, 3], [4, 5]], [], np.zeros(0))
+    _check(gpu, oracle, E, [1, -1], B, [-1, 2])
+
+
+@pytest.mark.parametrize("nranks", [2, 3, 4])
+def test_shards_reassemble_full_result(gpu, oracle, nranks):
+    (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
+    cls = gpu.blocksparse.BlockSparseF64
+    A, B = cls.from_blocks(sa, ca, a), cls.from_blocks(sb, cb, b)
+    full = gpu.blocksparse.contract(A, la, B, lb)
+    coords, chunks = [], []
+    for r in range(nranks):
+        s = gpu.blocksparse.contract_shard(A, la, B, lb, r, nranks)
+        coords += s.coords
+        chunks.append(s.to_numpy_data())
+    assert coords == full.coords
+    assert np.array_equal(np.concatenate(chunks), full.to_numpy_data())  # same kernel, same bits
+
+
+def test_cfg4_small_scale_vs_oracle(gpu, oracle):
+    """U(1) rank-4 x rank-4 over 2 shared indices, 9 sectors, dims / 8."""
+    A, B, la, lb = cfg4_tensors(scale=8)
+    _check(gpu, oracle, A, la, B, lb)
+
+
+def test_cfg4_half_scale_block_spot_checks(gpu):
+    """The primary configuration (sector dims halved, 4.25 GB per operand):
+    structure checked in full, block values against numpy on a sample of
+    output blocks (size-independent check of the full-size run)."""
+    (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=2)
+    cls = gpu.blocksparse.BlockSparseF64
+    A, B = cls.from_blocks(sa, ca, a), cls.from_blocks(sb, cb, b)
+    C = gpu.blocksparse.contract(A, la, B, lb)
+    assert C.coords == sorted(C.coords) and C.nnzblocks == 489
+    offs = np.cumsum([0] + [int(np.prod([sa[i][c[i]] for i in range(4)])) for c in ca])
+    amap = {c: i for i, c in enumerate(ca)}
+    bmap = {c: i for i, c in enumerate(cb)}
+    rng = np.random.default_rng(3)
+    coords = C.coords
+    for idx in rng.choice(len(coords), size=6, replace=False):
+        oc = coords[idx]
+        shape = (sa[0][oc[0]], sa[1][oc[1]], sb[2][oc[2]], sb[3][oc[3]])
+        ref = np.zeros(shape)
+        for (c, i) in amap.items():
+            if c[0] != oc[0] or c[1] != oc[1]:
+                continue
+            d = (c[2], c[3], oc[2], oc[3])
+            if d not in bmap:
+                continue
+            ash = tuple(sa[k][c[k]] for k in range(4))
+            bsh = tuple(sb[k][d[k]] for k in range(4))
+            ab = a[offs[i]:offs[i] + int(np.prod(ash))].reshape(ash, order="F")
+            j = bmap[d]
+            bb = b[offs[j]:offs[j] + int(np.prod(bsh))].reshape(bsh, order="F")
+            ref += np.einsum("ijkl,klmn->ijmn", ab, bb, optimize=True)
+        assert rel_fro(C.block(oc), ref) <= RTOL
+
+
+def test_permutedims_and_dense_roundtrip(gpu, oracle):
+    rng = np.random.default_rng(9)
+    for cplx in (False, True):
+        A = random_bs(rng, [[2, 3], [1, 4, 2], [3, 3]], 0.6, cplx)
+        cls = _cls(gpu, cplx)
+        t = cls.from_blocks(*A)
+        st, ref = oracle.bs_permutedims(oracle.BlockSparse(*A), [2, 0, 1])
+        p = t.permutedims([2, 0, 1])
+        assert p.coords == ref.coords and p.block_sizes == ref.block_sizes
+        assert np.array_equal(p.to_numpy_data(), ref.data)  # bit-exact
+        dense = t.to_dense().to_numpy()
+        assert np.array_equal(dense, oracle.bs_to_dense(oracle.BlockSparse(*A)))
+        back = cls.from_dense(t.to_dense(), A[0], A[1])
+        assert np.array_equal(back.to_numpy_data(), np.asarray(A[2]))
+    with pytest.raises(ValueError):
+        t.permutedims([0, 0, 1])
+
+
+def test_diag_to_dense_and_contract_diag(gpu, oracle):
+    rng = np.random.default_rng(10)
+    for cplx in (False, True):
+        dt = np.complex128 if cplx else np.float64
+        sizes = [[2, 3, 4], [2, 3, 4]]
+        coords = [(0, 0), (2, 2), (1, 1)]
+        diag = (rng.standard_normal(9) + (1j * rng.standard_normal(9) if cplx else 0)).astype(dt)
+        dcls = gpu.blocksparse.DiagBlockSparseC64 if cplx else gpu.blocksparse.DiagBlockSparseF64
+        S = dcls.from_blocks(sizes, coords, diag)
+        sd = S.to_dense().to_numpy()
+        assert np.array_equal(sd, oracle.diag_to_dense(sizes, coords, diag))
+        # fast path: A(1,2,-1) x S(-1,3) is a scaling of A's last axis
+        A = random_bs(rng, [[3, 2], [1, 1], [2, 3, 4]], 0.8, cplx)
+        cls = _cls(gpu, cplx)
+        got = gpu.blocksparse.contract_diag(cls.from_blocks(*A), [1, 2, -1], S, [-1, 3])
+        Sbs = oracle.bs_from_dense(sd, sizes, coords)
+        st, ref = oracle.bs_contract(oracle.BlockSparse(*A), [1, 2, -1], Sbs, [-1, 3])
+        assert st == 0 and got.coords == ref.coords
+        assert rel_fro(got.to_numpy_data(), ref.data) <= RTOL
+        # general path (contracted axis not last)
+        A2 = random_bs(rng, [[2, 3, 4], [3, 2]], 0.8, cplx)
+        got2 = gpu.blocksparse.contract_diag(cls.from_blocks(*A2), [-1, 1], S, [-1, 2])
+        st, ref2 = oracle.bs_contract(oracle.BlockSparse(*A2), [-1, 1], Sbs, [-1, 2])
+        assert st == 0 and got2.coords == ref2.coords
+        assert rel_fro(got2.to_numpy_data(), ref2.data) <= RTOL
+
+
+def test_cfg5_reduced_bond_chain_vs_oracle(gpu, oracle):
+    """The c128 two-site MPS chain (A . S) . B with bond 1024 (33 sectors)."""
+    A, S, B = cfg5_tensors(bond=1024)
+    bs = gpu.blocksparse
+    AS = bs.contract_diag(bs.BlockSparseC64.from_blocks(*A), [1, 2, -1],
+                          bs.DiagBlockSparseC64.from_blocks(*S), [-1, 3])
+    C = bs.contract(AS, [1, 2, -1], bs.BlockSparseC64.from_blocks(*B), [-1, 3, 4])
+    Sd = oracle.diag_to_dense(*S)
+    st, ASr = oracle.bs_contract(oracle.BlockSparse(*A), [1, 2, -1], oracle.bs_from_dense(Sd, S[0], S[1]), [-1, 3])
+    assert st == 0
+    st, Cr = oracle.bs_contract(ASr, [1, 2, -1], oracle.BlockSparse(*B), [-1, 3, 4])
+    assert st == 0
+    assert C.coords == Cr.coords and C.block_sizes == Cr.block_sizes
+    assert rel_fro(C.to_numpy_data(), Cr.data) <= RTOL

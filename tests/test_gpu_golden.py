@@ -14,8 +14,6 @@ CASES = [c for c in load_cases() if c["op"] not in ("strides", "cart_to_lin", "l
 def test_capi_known_answer(case, gpu, oracle):
     eng = CapiEngine(gpu)
     op = case["op"]
-    if (op.startswith("bs_") or op.startswith("diag")) and not hasattr(gpu, "blocksparse"):
-        pytest.skip("block-sparse C ABI not built yet")
     if op == "from_data":
         import ctypes
 
