@@ -374,8 +374,11 @@ def main():
     # ---- extras: complex permute and the dense f64 MPS merge (DMMA GEMM)
     extras = [batched_line]
     del src, dst
+    torch.cuda.empty_cache()
     if not args.no_extras:
-        extras += run_extras(args, torch, lib, ndt, stream, peaks)
+        if world == 1:
+            extras += run_extras(args, torch, lib, ndt, stream, peaks)
+        extras += run_blocksparse(args, torch, ndt, world, rank, pg)
 
     # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
     cpu = None
@@ -415,6 +418,89 @@ def main():
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+
+
+def run_blocksparse(args, torch, ndt, world, rank, pg):
+    """Block-sparse contractions (configs[3] at half scale, configs[4]) on
+    FP64 tensor cores; with N ranks each computes its FLOP-balanced share of
+    the output blocks (strong scaling: the total work is fixed)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import workloads as W
+
+    bs = ndt.blocksparse
+    out = []
+
+    def timed(fn, reps):
+        for _ in range(2):
+            r = fn()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            r = fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item()), r
+
+    # ---- configs[3]: U(1) rank-4 x rank-4, 9 sectors, dims halved
+    dims = W.cfg4_dims(2)
+    sizes, coords = W.cfg4_structure(dims)
+    total = sum(W.block_elems(sizes, coords))
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1004)
+    dA = torch.randn(total, dtype=torch.float64, device="cuda", generator=g)
+    dB = torch.randn(total, dtype=torch.float64, device="cuda", generator=g)
+    A = bs.BlockSparseF64.from_torch(sizes, coords, dA)
+    B = bs.BlockSparseF64.from_torch(sizes, coords, dB)
+    del dA, dB
+    la, lb = [1, 2, -1, -2], [-1, -2, 3, 4]
+    flops = W.flops_blocksparse((sizes, coords, None), la, (sizes, coords, None), lb, False)
+    if world == 1:
+        ms, _ = timed(lambda: bs.contract(A, la, B, lb), 3)
+    else:
+        ms, _ = timed(lambda: bs.contract_shard(A, la, B, lb, rank, world), 3)
+    tf = flops / (ms * 1e-3) / 1e12
+    out.append({"workload": "block-sparse U(1) rank-4 x rank-4 f64, sector dims halved [4,12,28,48,72,48,28,12,4] "
+                            "(489 blocks, 4.25 GB per operand)",
+                "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": flops, "n_gpus": world,
+                "scaling": "strong" if world > 1 else None,
+                "roofline": {"bound": "fp64_tensor", "achieved": tf / world, "peak": FP64_DMMA_PEAK_TFLOPS,
+                             "unit": "TFLOP/s per GPU", "frac": tf / world / FP64_DMMA_PEAK_TFLOPS}})
+    del A, B
+    torch.cuda.empty_cache()
+
+    # ---- configs[4]: c128 two-site MPS (A . S) . B, bond 8192, 33 sectors
+    (sa, ca, a), (ss, cs_, sd), (sb, cb, b) = W.cfg5_tensors()
+    A = bs.BlockSparseC64.from_blocks(sa, ca, a)
+    S = bs.DiagBlockSparseC64.from_blocks(ss, cs_, sd)
+    B = bs.BlockSparseC64.from_blocks(sb, cb, b)
+    flops5 = W.flops_blocksparse((sa, ca, None), [1, 2, -1], (sb, cb, None), [-1, 3, 4], True)
+
+    def chain():
+        AS = bs.contract_diag(A, [1, 2, -1], S, [-1, 3])
+        if world == 1:
+            return bs.contract(AS, [1, 2, -1], B, [-1, 3, 4])
+        return bs.contract_shard(AS, [1, 2, -1], B, [-1, 3, 4], rank, world)
+
+    ms5, _ = timed(chain, 10)
+    tf5 = flops5 / (ms5 * 1e-3) / 1e12
+    entry = {"workload": "block-sparse c128 two-site MPS (A.S).B, bond 8192 in 33 sectors, DiagBlockSparse S",
+             "value": tf5, "unit": "TFLOP/s", "ms": ms5, "flop": flops5, "n_gpus": world,
+             "scaling": "strong" if world > 1 else None, "gather": "none (compute only)",
+             "roofline": {"bound": "fp64_tensor", "achieved": tf5 / world, "peak": FP64_DMMA_PEAK_TFLOPS,
+                          "unit": "TFLOP/s per GPU", "frac": tf5 / world / FP64_DMMA_PEAK_TFLOPS}}
+    out.append(entry)
+    if world > 1:
+        msg, _ = timed(lambda: bs.allgather(chain()), 5)
+        out.append({"workload": "block-sparse c128 two-site MPS, sharded + NCCL allgather of the output",
+                    "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": msg, "n_gpus": world,
+                    "scaling": "strong", "gather": "allgather (NCCL) of all output blocks to every rank"})
+    return out
 
 
 def run_extras(args, torch, lib, ndt, stream, peaks):

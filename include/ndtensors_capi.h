@@ -177,6 +177,11 @@ ndt_blocksparse_f64* ndt_blocksparse_f64_zeros(size_t ndim, const size_t* nblock
 ndt_blocksparse_f64* ndt_blocksparse_f64_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
                                                    size_t nnzb, const size_t* coords, const double* data, size_t len,
                                                    int* status);
+/* as from_data, copying from device memory of the current device */
+ndt_blocksparse_f64* ndt_blocksparse_f64_from_device_ptr(size_t ndim, const size_t* nblocks,
+                                                         const size_t* block_sizes, size_t nnzb,
+                                                         const size_t* coords, const double* dptr, size_t len,
+                                                         int* status);
 void ndt_blocksparse_f64_release(ndt_blocksparse_f64* t);
 size_t ndt_blocksparse_f64_ndim(const ndt_blocksparse_f64* t);
 size_t ndt_blocksparse_f64_nnzblocks(const ndt_blocksparse_f64* t); /* nnzblocks (blocksparse_tensor.rs:99) */
@@ -223,6 +228,10 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_zeros(size_t ndim, const size_t* nblock
 ndt_blocksparse_c64* ndt_blocksparse_c64_from_data(size_t ndim, const size_t* nblocks, const size_t* block_sizes,
                                                    size_t nnzb, const size_t* coords, const double* data, size_t len,
                                                    int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_from_device_ptr(size_t ndim, const size_t* nblocks,
+                                                         const size_t* block_sizes, size_t nnzb,
+                                                         const size_t* coords, const double* dptr, size_t len,
+                                                         int* status);
 void ndt_blocksparse_c64_release(ndt_blocksparse_c64* t);
 size_t ndt_blocksparse_c64_ndim(const ndt_blocksparse_c64* t);
 size_t ndt_blocksparse_c64_nnzblocks(const ndt_blocksparse_c64* t);

@@ -789,6 +789,19 @@ extern "C" {
     }                                                                                                                \
     return (T*)bs_new(DTYPE_##DT, ndim, nblocks, block_sizes, nnzb, coords, data, len, status);                      \
   }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_from_device_ptr(size_t ndim, const size_t* nblocks, const size_t* block_sizes,           \
+                                            size_t nnzb, const size_t* coords, const double* dptr, size_t len,       \
+                                            int* status) {                                                           \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
+      if (!dptr) throw Error(ErrKind::InvalidArgument, "NULL device pointer");                                       \
+      std::vector<std::vector<size_t>> bsz, cs;                                                                      \
+      read_structure(ndim, nblocks, block_sizes, nnzb, coords, &bsz, &cs);                                           \
+      BlockSparseT t = make_bs(DTYPE_##DT, bsz, cs);                                                                 \
+      if (len != t.total()) throw Error(ErrKind::ShapeMismatch, "data length != total block elements");              \
+      if (len) t.st = make_from_device(DTYPE_##DT, dptr, len, {len}).st;                                             \
+      return new NdtBs{t};                                                                                           \
+    });                                                                                                              \
+  }                                                                                                                  \
   void ndt_blocksparse_##DT##_release(T* t) { delete (NdtBs*)t; }                                                    \
   size_t ndt_blocksparse_##DT##_ndim(const T* t) { return t ? ((const NdtBs*)t)->t.ndim() : 0; }                     \
   size_t ndt_blocksparse_##DT##_nnzblocks(const T* t) { return t ? ((const NdtBs*)t)->t.nnzb() : 0; }                \

@@ -100,6 +100,8 @@ SIGNATURES = [
             (f"ndt_blocksparse_{dt}_zeros", vp, [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_int_p]),
             (f"ndt_blocksparse_{dt}_from_data", vp,
              [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_double_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_blocksparse_{dt}_from_device_ptr", vp,
+             [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, vp, ctypes.c_size_t, c_int_p]),
             (f"ndt_blocksparse_{dt}_release", None, [vp]),
             (f"ndt_blocksparse_{dt}_ndim", ctypes.c_size_t, [vp]),
             (f"ndt_blocksparse_{dt}_nnzblocks", ctypes.c_size_t, [vp]),

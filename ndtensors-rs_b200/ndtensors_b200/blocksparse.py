@@ -77,6 +77,23 @@ class _BsBase:
         return cls(p)
 
     @classmethod
+    def from_torch(cls, block_sizes, coords, data):
+        """Packed data from a CUDA torch tensor (copied device to device)."""
+        import torch
+
+        want = torch.complex128 if cls._width == 2 else torch.float64
+        d = data.to(want).contiguous()
+        ndim, nblk, bsz, nnzb, cs = _structure_args(block_sizes, coords)
+        st = ctypes.c_int(-999)
+        p = getattr(get_lib(), f"ndt_blocksparse_{cls._prefix}_from_device_ptr")(
+            ndim, nblk, bsz, nnzb, cs, ctypes.c_void_p(d.data_ptr()), d.numel(), ctypes.byref(st))
+        _raise(st.value, "blocksparse from_device_ptr")
+        return cls(p)
+
+    def device_ptr(self) -> int:
+        return self._f("device_ptr")(self._ptr)
+
+    @classmethod
     def from_dense(cls, dense, block_sizes, coords):
         ndim, nblk, bsz, nnzb, cs = _structure_args(block_sizes, coords)
         st = ctypes.c_int(-999)
