@@ -12,11 +12,15 @@
 //     the sum over its matched block pairs ("segments") of A_s B_s.  A CTA
 //     owns one output tile and accumulates every segment in registers, so
 //     accumulation is deterministic and needs no atomics.
-// Operands are staged global -> shared with cp.async in a multi-stage ring;
-// shared tiles use padded pitches (4 mod 16 doubles for f64; 2 / 4 mod 8
-// complex elements) so fragment loads are bank-conflict free.  Complex128
-// uses the 4M real decomposition inside the kernel (Cr += Ar Br - Ai Bi,
-// Ci += Ar Bi + Ai Br) on interleaved (re, im) data.
+// Operands are staged global -> shared with cp.async in a multi-stage ring.
+// Each thread's copies follow a fixed pattern: a constant column within a
+// shared row and a constant row step per copy, so a copy costs one pointer
+// add and two compares.  f64 operands whose bases, offsets and leading
+// dimensions are 16-byte aligned move as 16-byte pairs (VEC).  Shared tiles
+// use padded pitches (4 mod 16 doubles for f64; 2 / 4 mod 8 complex elements
+// for MN- / K-major) so the fragment loads are bank-conflict free.
+// Complex128 uses the 4M real decomposition inside the kernel
+// (Cr += Ar Br - Ai Bi, Ci += Ar Bi + Ai Br) on interleaved (re, im) data.
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -46,10 +50,11 @@ __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pre
   int sz = pred ? 8 : 0;
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
 }
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+// 16-byte copy of which only the first `bytes` (0, 8 or 16) are read; the
+// rest of the 16 bytes is zero-filled.
+__device__ __forceinline__ void cp_async16n(void* smem, const void* gmem, int bytes) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  int sz = pred ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(sz));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(bytes));
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 template <int N>
@@ -92,12 +97,28 @@ struct Cfg {
   static constexpr size_t smem_bytes = (size_t)STAGES * stage_elems * ES;
 };
 
-template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM>
+// Copy pattern of one operand tile: ROWS x CONT elements in shared memory
+// (CONT contiguous), PW elements per copy.
+template <int ROWS, int CONT, int PW, int NTH>
+struct CopyPlan {
+  static constexpr int CW = CONT / PW;         // copies per shared row
+  static constexpr int RS = NTH / CW;          // rows advanced per copy
+  static constexpr int IT = ROWS * CW / NTH;   // copies per thread per stage
+  static_assert(NTH % CW == 0 && (ROWS * CW) % NTH == 0, "tile not divisible by threads");
+};
+
+// VEC (f64 only): 16-byte pair copies along the contiguous index; a pair
+// crossing the matrix edge copies 8 bytes and zero-fills the rest.
+template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
+          bool GROUPED>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(const __grid_constant__ KArgs args) {
   using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM>;
   constexpr int NTH = C::kThreads, MT = C::MT, NT = C::NT, ES = C::ES;
   constexpr int LDA = C::PA::value, LDB = C::PB::value;
   constexpr int RPL = CPLX ? 2 : 1;  // doubles per element
+  constexpr int PW = (!CPLX && VEC) ? 2 : 1;
+  using PlanA = CopyPlan<AK ? BM : BK, AK ? BK : BM, PW, NTH>;
+  using PlanB = CopyPlan<BKM ? BN : BK, BKM ? BK : BN, PW, NTH>;
   extern __shared__ __align__(16) double smem[];
 
   const int tid = threadIdx.x;
@@ -111,7 +132,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
   int64_t m0, n0;
   const char* Ab = (const char*)args.A;
   const char* Bb = (const char*)args.B;
-  if (args.tiles == nullptr) {
+  if constexpr (!GROUPED) {
     // dense: rasterise with groups of 8 tile-rows for L2 reuse
     int bid = blockIdx.x;
     const int GROUP = 8;
@@ -142,13 +163,17 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
     n0 = (int64_t)td.z * BN;
   }
 
+  // ---- per-thread copy geometry (constant over the launch)
+  const int a_c = (tid % PlanA::CW) * PW, a_r = tid / PlanA::CW;
+  const int b_c = (tid % PlanB::CW) * PW, b_r = tid / PlanB::CW;
+  // Rows of the tile that exist in the matrix for the M / N side: fixed per tile.
+  const int64_t a_mrem = m - m0, b_nrem = n - n0;
+
   // ---- load iterator over (segment, k0)
   int64_t seg = seg_begin, seg_end = seg_begin + seg_count;
   int64_t a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0;
   auto load_seg = [&](int64_t s) {
-    if (args.tiles == nullptr) {
-      a_off = 0;
-      b_off = 0;
+    if constexpr (!GROUPED) {
       kseg = args.k;
       lda = args.lda;
       ldb = args.ldb;
@@ -161,77 +186,78 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
       ldb = sd.ldb;
     }
   };
-  int64_t total_steps = 0;
-  if (args.tiles == nullptr) {
-    total_steps = (args.k + BK - 1) / BK;
+  int total_steps = 0;
+  if constexpr (!GROUPED) {
+    total_steps = (int)((args.k + BK - 1) / BK);
   } else {
-    for (int64_t s = seg_begin; s < seg_end; s++) total_steps += (args.segs[s].k + BK - 1) / BK;
+    for (int64_t s = seg_begin; s < seg_end; s++) total_steps += (int)((args.segs[s].k + BK - 1) / BK);
   }
   if (seg < seg_end) load_seg(seg);
 
   auto issue_load = [&](int stage) {
     double* As = smem + (size_t)stage * C::stage_elems * RPL;
     double* Bs = As + (size_t)C::PA::elems * RPL;
-    const char* Ag = Ab + a_off * ES;
-    const char* Bg = Bb + b_off * ES;
-    // A tile: BM x BK
-    static_assert((BM * BK) % NTH == 0 && (BN * BK) % NTH == 0, "tile not divisible by threads");
+    const int64_t krem = kseg - k0;  // k rows left in this segment
+    // ---- A: rows are M (AK) or K (MN-major); the contiguous index is the other
+    {
+      const int64_t cont_rem = AK ? krem - a_c : a_mrem - a_c;  // valid contiguous elements from a_c
+      const int nv = cont_rem >= PW ? PW : (cont_rem > 0 ? (int)cont_rem : 0);
+      const int64_t row_rem = (AK ? a_mrem : krem) - a_r;
+      const char* src = Ab + (a_off + (AK ? (k0 + a_c) + (m0 + a_r) * lda : (m0 + a_c) + (k0 + a_r) * lda)) * ES;
+      const int64_t rstep = (int64_t)PlanA::RS * lda * ES;
+      double* dst = As + ((size_t)a_r * LDA + a_c) * RPL;
 #pragma unroll
-    for (int it = 0; it < (BM * BK) / NTH; it++) {
-      const int e = tid + it * NTH;
-      int r, c;  // r: row in smem, c: contiguous column in smem
-      int64_t gi, gl;
-      if (AK) {
-        r = e / BK;
-        c = e % BK;
-        gi = m0 + r;
-        gl = k0 + c;
-      } else {
-        r = e / BM;
-        c = e % BM;
-        gl = k0 + r;
-        gi = m0 + c;
+      for (int it = 0; it < PlanA::IT; it++) {
+        const bool rok = it * PlanA::RS < row_rem;
+        const int nb = rok ? nv : 0;
+        const char* p = nb ? src + it * rstep : Ab;
+        double* d = dst + (size_t)it * PlanA::RS * LDA * RPL;
+        if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
+        else if constexpr (CPLX)
+          cp_async16n(d, p, nb * 16);
+        else
+          cp_async8(d, p, nb != 0);
       }
-      bool ok = gi < m && gl < kseg;
-      const char* src = ok ? Ag + (AK ? (gl + gi * lda) : (gi + gl * lda)) * ES : Ag;
-      double* dst = As + ((size_t)r * LDA + c) * RPL;
-      if (CPLX)
-        cp_async16(dst, src, ok);
-      else
-        cp_async8(dst, src, ok);
     }
-    // B tile: BK x BN
+    // ---- B: rows are N (BKM) or K (MN-major)
+    {
+      const int64_t cont_rem = BKM ? krem - b_c : b_nrem - b_c;
+      const int nv = cont_rem >= PW ? PW : (cont_rem > 0 ? (int)cont_rem : 0);
+      const int64_t row_rem = (BKM ? b_nrem : krem) - b_r;
+      const char* src = Bb + (b_off + (BKM ? (k0 + b_c) + (n0 + b_r) * ldb : (n0 + b_c) + (k0 + b_r) * ldb)) * ES;
+      const int64_t rstep = (int64_t)PlanB::RS * ldb * ES;
+      double* dst = Bs + ((size_t)b_r * LDB + b_c) * RPL;
 #pragma unroll
-    for (int it = 0; it < (BN * BK) / NTH; it++) {
-      const int e = tid + it * NTH;
-      int r, c;
-      int64_t gj, gl;
-      if (BKM) {
-        r = e / BK;
-        c = e % BK;
-        gj = n0 + r;
-        gl = k0 + c;
-      } else {
-        r = e / BN;
-        c = e % BN;
-        gl = k0 + r;
-        gj = n0 + c;
+      for (int it = 0; it < PlanB::IT; it++) {
+        const bool rok = it * PlanB::RS < row_rem;
+        const int nb = rok ? nv : 0;
+        const char* p = nb ? src + it * rstep : Bb;
+        double* d = dst + (size_t)it * PlanB::RS * LDB * RPL;
+        if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
+        else if constexpr (CPLX)
+          cp_async16n(d, p, nb * 16);
+        else
+          cp_async8(d, p, nb != 0);
       }
-      bool ok = gj < n && gl < kseg;
-      const char* src = ok ? Bg + (BKM ? (gl + gj * ldb) : (gj + gl * ldb)) * ES : Bg;
-      double* dst = Bs + ((size_t)r * LDB + c) * RPL;
-      if (CPLX)
-        cp_async16(dst, src, ok);
-      else
-        cp_async8(dst, src, ok);
     }
+  };
+  // Loads still to issue: dense runs k0 to kseg; grouped walks the segments.
+  auto more = [&]() -> bool {
+    if constexpr (!GROUPED)
+      return k0 < kseg;
+    else
+      return seg < seg_end;
   };
   auto advance = [&]() {
     k0 += BK;
-    if (k0 >= kseg) {
-      seg++;
-      k0 = 0;
-      if (seg < seg_end) load_seg(seg);
+    if constexpr (GROUPED) {
+      if (k0 >= kseg) {
+        seg++;
+        k0 = 0;
+        if (seg < seg_end) load_seg(seg);
+      }
     }
   };
 
@@ -246,25 +272,23 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
   // ---- prologue
 #pragma unroll
   for (int s = 0; s < STAGES - 1; s++) {
-    if (seg < seg_end) {
+    if (more()) {
       issue_load(s);
       advance();
     }
     cp_commit();
   }
 
-  for (int64_t step = 0; step < total_steps; step++) {
+  int cs = 0, ls = STAGES - 1;  // stage computed / stage loaded
+  for (int step = 0; step < total_steps; step++) {
     cp_wait<STAGES - 2>();
     __syncthreads();
-    {
-      int ls = (int)((step + STAGES - 1) % STAGES);
-      if (seg < seg_end) {
-        issue_load(ls);
-        advance();
-      }
-      cp_commit();
+    if (more()) {
+      issue_load(ls);
+      advance();
     }
-    const int cs = (int)(step % STAGES);
+    cp_commit();
+    ls = (ls + 1 == STAGES) ? 0 : ls + 1;
     const double* As = smem + (size_t)cs * C::stage_elems * RPL;
     const double* Bs = As + (size_t)C::PA::elems * RPL;
 #pragma unroll
@@ -326,6 +350,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
           }
       }
     }
+    cs = (cs + 1 == STAGES) ? 0 : cs + 1;
   }
   cp_wait<0>();
 
@@ -359,10 +384,10 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
       }
 }
 
-template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM>
-void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED>
+void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
   using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM>;
-  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM>;
+  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED>;
   static bool attr = false;
   if (!attr) {
     NDT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem_bytes));
@@ -373,35 +398,58 @@ void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
   NDT_CUDA(cudaGetLastError());
 }
 
-// Tile configurations.  "Big": 128x128 (f64) / 64x128 (c128) per CTA, 8
-// warps; "small": 64x64 (f64) / 32x64 (c128), 4 warps, for grids that would
-// otherwise leave SMs idle.
-template <bool CPLX, bool AK, bool BKM>
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC>
+void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
+  if (a.tiles == nullptr)
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, false>(a, grid, s);
+  else
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true>(a, grid, s);
+}
+
+// Tile configurations (chosen by a sweep on B200).  f64: 128x128x32 (8
+// warps, 3 stages) or 64x64x32 (4 warps, 3 stages, two CTAs per SM) for grids
+// that would otherwise leave SMs idle; c128: 64x128x16 / 32x64x16.
+template <bool CPLX, bool AK, bool BKM, bool VEC>
 void launch(const KArgs& a, int grid, bool small, cudaStream_t s) {
-  if (!CPLX) {
+  if constexpr (!CPLX) {
     if (small)
-      launch_cfg<false, 64, 64, 16, 2, 2, 4, AK, BKM>(a, grid, s);
+      launch_cfg<false, 64, 64, 32, 2, 2, 3, AK, BKM, VEC>(a, grid, s);
     else
-      launch_cfg<false, 128, 128, 16, 2, 4, 4, AK, BKM>(a, grid, s);
+      launch_cfg<false, 128, 128, 32, 2, 4, 3, AK, BKM, VEC>(a, grid, s);
   } else {
     if (small)
-      launch_cfg<true, 32, 64, 16, 1, 2, 3, AK, BKM>(a, grid, s);
+      launch_cfg<true, 32, 64, 16, 1, 2, 3, AK, BKM, false>(a, grid, s);
     else
-      launch_cfg<true, 64, 128, 16, 2, 4, 3, AK, BKM>(a, grid, s);
+      launch_cfg<true, 64, 128, 16, 2, 4, 3, AK, BKM, false>(a, grid, s);
   }
 }
 
 template <bool CPLX>
-void dispatch(const KArgs& a, int grid, bool small, bool ak, bool bk, cudaStream_t s) {
+void dispatch(const KArgs& a, int grid, bool small, bool ak, bool bk, bool vec, cudaStream_t s) {
+  if (!CPLX && vec) {
+    if (ak && bk)
+      launch<CPLX, true, true, true>(a, grid, small, s);
+    else if (ak && !bk)
+      launch<CPLX, true, false, true>(a, grid, small, s);
+    else if (!ak && bk)
+      launch<CPLX, false, true, true>(a, grid, small, s);
+    else
+      launch<CPLX, false, false, true>(a, grid, small, s);
+    return;
+  }
   if (ak && bk)
-    launch<CPLX, true, true>(a, grid, small, s);
+    launch<CPLX, true, true, false>(a, grid, small, s);
   else if (ak && !bk)
-    launch<CPLX, true, false>(a, grid, small, s);
+    launch<CPLX, true, false, false>(a, grid, small, s);
   else if (!ak && bk)
-    launch<CPLX, false, true>(a, grid, small, s);
+    launch<CPLX, false, true, false>(a, grid, small, s);
   else
-    launch<CPLX, false, false>(a, grid, small, s);
+    launch<CPLX, false, false, false>(a, grid, small, s);
 }
+
+// 16-byte pair copies need 16-byte aligned operand bases and even element
+// offsets / leading dimensions.
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 void tile_dims(bool cplx, bool small, int* bm, int* bn) {
   if (!cplx) {
@@ -450,10 +498,11 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   a.tiles = nullptr;
   a.accumulate = accumulate ? 1 : 0;
   int grid = a.mtiles * a.ntiles_n;
+  const bool vec = aligned16(A.ptr) && aligned16(B.ptr) && A.ld % 2 == 0 && B.ld % 2 == 0;
   if (cplx)
-    dispatch<true>(a, grid, small, A.kmajor, B.kmajor, s);
+    dispatch<true>(a, grid, small, A.kmajor, B.kmajor, false, s);
   else
-    dispatch<false>(a, grid, small, A.kmajor, B.kmajor, s);
+    dispatch<false>(a, grid, small, A.kmajor, B.kmajor, vec, s);
 }
 
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
@@ -513,10 +562,13 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.segs = (const GroupedSegment*)(d + off_s);
   a.accumulate = 0;
   int grid = (int)tiles.size();
+  bool vec = aligned16(A) && aligned16(B);
+  for (const GroupedSegment& sg : segs)
+    vec = vec && sg.a_off % 2 == 0 && sg.b_off % 2 == 0 && sg.lda % 2 == 0 && sg.ldb % 2 == 0;
   if (cplx)
-    dispatch<true>(a, grid, small, a_kmajor, b_kmajor, s);
+    dispatch<true>(a, grid, small, a_kmajor, b_kmajor, false, s);
   else
-    dispatch<false>(a, grid, small, a_kmajor, b_kmajor, s);
+    dispatch<false>(a, grid, small, a_kmajor, b_kmajor, vec, s);
   NDT_CUDA(cudaFreeAsync(d, s));
 }
 
