@@ -304,46 +304,70 @@ def shard_plan(a, labels_a, b, labels_b, nranks: int):
     return [int(x) for x in blocks], [float(x) for x in flops]
 
 
+class _DeviceSpan:
+    """A raw device range exposed through __cuda_array_interface__ (zero copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f8", "data": (int(ptr), False),
+                                         "strides": None, "version": 2}
+
+
 def allgather(shard, group=None):
     """Gather every rank's shard (disjoint output blocks of one contraction)
-    into the full block-sparse tensor on all ranks, with torch.distributed
-    (NCCL over NVLink on GPUs, gloo on CPU).  Blocks come out sorted, as
-    contract_blocksparse orders them."""
+    into the full block-sparse tensor on all ranks, with torch.distributed.
+    Blocks come out sorted, as contract_blocksparse orders them.
+
+    Shards are contiguous ranges of the sorted output block list, so rank r's
+    packed data is the r-th contiguous range of the gathered data.  On NCCL
+    the data stays in HBM: each rank's range is broadcast from that rank
+    straight into its place in one device buffer (no padding, no host copy);
+    on gloo (CPU tests) the ranges go through host memory."""
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
-    dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" else torch.device("cpu")
+    nccl = dist.get_backend(group) == "nccl"
+    dev = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
     sizes, coords, _ = shard._structure()
     nd = len(sizes)
-    data = shard.to_numpy_data()
     width = shard._width
-    meta = torch.tensor([len(coords), data.size], dtype=torch.int64, device=dev)
+    nelem = shard.nnz
+    meta = torch.tensor([len(coords), nelem], dtype=torch.int64, device=dev)
     metas = [torch.zeros_like(meta) for _ in range(world)]
     dist.all_gather(metas, meta, group=group)
-    nb_max = max(int(m[0]) for m in metas)
-    nd_max = max(int(m[1]) for m in metas)
+    counts = [(int(m[0]), int(m[1])) for m in metas]
+    nb_max = max(c[0] for c in counts)
     c_t = torch.full((max(nb_max, 1), nd), -1, dtype=torch.int64, device=dev)
     if coords:
         c_t[: len(coords)] = torch.tensor(coords, dtype=torch.int64, device=dev)
-    d_t = torch.zeros(max(nd_max, 1) * width, dtype=torch.float64, device=dev)
-    if data.size:
-        d_t[: data.size * width] = torch.from_numpy(np.ascontiguousarray(data).view(np.float64)).to(dev)
     cs = [torch.empty_like(c_t) for _ in range(world)]
-    ds = [torch.empty_like(d_t) for _ in range(world)]
     dist.all_gather(cs, c_t, group=group)
-    dist.all_gather(ds, d_t, group=group)
-    all_coords, chunks = [], []
+    all_coords = []
     for r in range(world):
-        nbr, ndr = int(metas[r][0]), int(metas[r][1])
-        all_coords += [tuple(int(x) for x in row) for row in cs[r][:nbr].cpu().tolist()]
-        chunks.append(ds[r][: ndr * width].cpu().numpy())
-    flat = np.concatenate(chunks) if chunks else np.zeros(0)
-    if width == 2:
-        flat = flat.view(np.complex128)
-    # shards are contiguous ranges of the sorted block list, gathered in rank
-    # order, so the concatenation is already sorted and packed
-    return type(shard).from_blocks(sizes, all_coords, flat)
+        all_coords += [tuple(int(x) for x in row) for row in cs[r][: counts[r][0]].cpu().tolist()]
+    offs = [0]
+    for _, ne in counts:
+        offs.append(offs[-1] + ne * width)
+    rank = dist.get_rank(group)
+    full = torch.empty(max(offs[-1], 1), dtype=torch.float64, device=dev)
+    if nelem:
+        if nccl:
+            # the shard was written on the library's stream
+            check_status(get_lib().ndt_b200_synchronize(), "synchronize")
+            own = torch.as_tensor(_DeviceSpan(shard.device_ptr(), nelem * width), device=dev)
+        else:
+            own = torch.from_numpy(np.ascontiguousarray(shard.to_numpy_data()).view(np.float64))
+        full[offs[rank]: offs[rank + 1]].copy_(own)
+    for r in range(world):
+        if offs[r + 1] > offs[r]:
+            src = dist.get_global_rank(group, r) if group is not None else r
+            dist.broadcast(full[offs[r]: offs[r + 1]], src=src, group=group)
+    if nccl:
+        torch.cuda.current_stream().synchronize()
+        data = full[: offs[-1]]
+        return type(shard).from_torch(sizes, all_coords, data.view(torch.complex128) if width == 2 else data)
+    flat = full[: offs[-1]].numpy()
+    return type(shard).from_blocks(sizes, all_coords, flat.view(np.complex128) if width == 2 else flat)
 
 
 def contract_diag(a, labels_a, s, labels_s):

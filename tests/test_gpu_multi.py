@@ -1,0 +1,90 @@
+"""Sharded block-sparse contraction on 2 GPUs over NCCL.
+
+Each rank computes its FLOP-balanced share of the output blocks
+(contract_shard) and the shards are gathered in HBM (allgather: one NCCL
+broadcast per rank into a single device buffer).  The gathered tensor must
+equal the unsharded contraction on one GPU.  Runs as two spawned processes,
+one per GPU; skipped when fewer than two devices are visible.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "ndtensors-rs_b200"))
+    sys.path.insert(0, os.path.join(root, "tests"))
+    import ndtensors_b200 as ndt
+    from workloads import cfg4_tensors, cfg5_tensors
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    bs = ndt.blocksparse
+    results = []
+    try:
+        # U(1) rank-4 x rank-4, sector dims / 8 (f64)
+        (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
+        A = bs.BlockSparseF64.from_blocks(sa, ca, a)
+        B = bs.BlockSparseF64.from_blocks(sb, cb, b)
+        full = bs.contract(A, la, B, lb)
+        shard = bs.contract_shard(A, la, B, lb, rank, world)
+        gathered = bs.allgather(shard)
+        ok = gathered.coords == full.coords and np.allclose(
+            gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
+        results.append(("cfg4/8 f64", bool(ok), shard.nnzblocks, full.nnzblocks))
+        # c128 two-site MPS chain with the diagonal bond tensor, bond 1024
+        (sa, ca, a), (ss, cs_, sd), (sb, cb, b) = cfg5_tensors(bond=1024)
+        A = bs.BlockSparseC64.from_blocks(sa, ca, a)
+        S = bs.DiagBlockSparseC64.from_blocks(ss, cs_, sd)
+        B = bs.BlockSparseC64.from_blocks(sb, cb, b)
+        AS = bs.contract_diag(A, [1, 2, -1], S, [-1, 3])
+        full = bs.contract(AS, [1, 2, -1], B, [-1, 3, 4])
+        gathered = bs.allgather(bs.contract_shard(AS, [1, 2, -1], B, [-1, 3, 4], rank, world))
+        ok = gathered.coords == full.coords and np.allclose(
+            gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
+        results.append(("cfg5 bond 1024 c128", bool(ok), -1, full.nnzblocks))
+        q.put((rank, results, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, results, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_contract_allgather_nccl_2gpu(gpu):
+    import multiprocessing as mp
+
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two visible GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = [q.get(timeout=300) for _ in ps]
+    for p in ps:
+        p.join(timeout=60)
+    for rank, results, err in out:
+        assert err is None, f"rank {rank}: {err}"
+        for name, ok, _, _ in results:
+            assert ok, f"rank {rank}: {name} gathered shards differ from the unsharded contraction"
