@@ -39,7 +39,28 @@ SHAPE = (16,) * 6
 PERM = (5, 3, 1, 0, 4, 2)
 NELEM = 16**6
 BYTES_F64 = 2 * NELEM * 8  # algorithmic bytes per tensor (read + write)
-FP64_DMMA_PEAK_TFLOPS = 37.1  # measured mma.sync f64 microbenchmark on this pool's B200 (profiles/fp64_peak.txt)
+_FP64_PEAK = {}
+
+
+def fp64_peak(stream=None):
+    """FP64 tensor-core peak (TFLOP/s) measured live on this GPU by a
+    register-only mma.sync f64 microbenchmark (csrc/fp64_peak.cu)."""
+    if "v" not in _FP64_PEAK:
+        lib = ctypes.CDLL(str(ROOT / "ndtensors-rs_b200" / "lib" / "libndt_fp64_peak.so"))
+        lib.ndt_fp64_tensor_peak_tflops.restype = ctypes.c_double
+        lib.ndt_fp64_tensor_peak_tflops.argtypes = [ctypes.c_void_p]
+        v = lib.ndt_fp64_tensor_peak_tflops(ctypes.c_void_p(stream.cuda_stream if stream is not None else 0))
+        if v <= 0:
+            raise RuntimeError("FP64 peak microbenchmark failed")
+        _FP64_PEAK["v"] = v
+    return _FP64_PEAK["v"]
+
+
+def fp64_roofline(tflops_per_gpu):
+    p = fp64_peak()
+    return {"bound": "fp64_tensor", "achieved": tflops_per_gpu, "peak": p, "unit": "TFLOP/s per GPU",
+            "frac": tflops_per_gpu / p,
+            "peak_source": "live mma.sync f64 register-only microbenchmark (csrc/fp64_peak.cu), measured"}
 
 
 def log(*a):
@@ -376,8 +397,10 @@ def main():
     del src, dst
     torch.cuda.empty_cache()
     if not args.no_extras:
+        fp64_peak(stream)
         if world == 1:
             extras += run_extras(args, torch, lib, ndt, stream, peaks)
+            extras += run_dmrg(args, torch, ndt, peaks)
         extras += run_blocksparse(args, torch, ndt, world, rank, pg)
 
     # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
@@ -469,8 +492,7 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
                             "(489 blocks, 4.25 GB per operand)",
                 "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": flops, "n_gpus": world,
                 "scaling": "strong" if world > 1 else None,
-                "roofline": {"bound": "fp64_tensor", "achieved": tf / world, "peak": FP64_DMMA_PEAK_TFLOPS,
-                             "unit": "TFLOP/s per GPU", "frac": tf / world / FP64_DMMA_PEAK_TFLOPS}})
+                "roofline": fp64_roofline(tf / world)})
     del A, B
     torch.cuda.empty_cache()
 
@@ -492,8 +514,7 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     entry = {"workload": "block-sparse c128 two-site MPS (A.S).B, bond 8192 in 33 sectors, DiagBlockSparse S",
              "value": tf5, "unit": "TFLOP/s", "ms": ms5, "flop": flops5, "n_gpus": world,
              "scaling": "strong" if world > 1 else None, "gather": "none (compute only)",
-             "roofline": {"bound": "fp64_tensor", "achieved": tf5 / world, "peak": FP64_DMMA_PEAK_TFLOPS,
-                          "unit": "TFLOP/s per GPU", "frac": tf5 / world / FP64_DMMA_PEAK_TFLOPS}}
+             "roofline": fp64_roofline(tf5 / world)}
     out.append(entry)
     if world > 1:
         msg, _ = timed(lambda: bs.allgather(chain()), 5)
@@ -560,9 +581,7 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
     out.append({"workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
                 "value": tf, "unit": "TFLOP/s", "ms": t,
-                "roofline": {"bound": "fp64_tensor", "achieved": tf, "peak": FP64_DMMA_PEAK_TFLOPS, "unit": "TFLOP/s",
-                             "frac": tf / FP64_DMMA_PEAK_TFLOPS,
-                             "peak_source": "measured mma.sync.m16n8k8.f64 register-only microbenchmark"}})
+                "roofline": fp64_roofline(tf)})
     # a large square f64 GEMM for the kernel's steady-state rate
     m = n = k = 4096
     A = torch.randn(m * k, dtype=torch.float64, device="cuda")
@@ -579,9 +598,71 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     t = a.elapsed_time(b) / 5
     tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
     out.append({"workload": "f64 GEMM 4096^3 (DMMA kernel steady state)", "value": tf, "unit": "TFLOP/s",
-                "roofline": {"bound": "fp64_tensor", "achieved": tf, "peak": FP64_DMMA_PEAK_TFLOPS,
-                             "unit": "TFLOP/s", "frac": tf / FP64_DMMA_PEAK_TFLOPS}})
+                "roofline": fp64_roofline(tf)})
     return out
+
+
+def run_dmrg(args, torch, ndt, peaks):
+    """DMRG environment-update chain, bond 1024: T1 = L.psi, T2 = T1.W1,
+    T3 = T2.W2, E = T3.R through contract_gemm (8.67e10 flop).  Steps 1 and 4
+    are DMMA GEMMs (step 4 packs its permuted operand); steps 2 and 3 run on
+    the skinny kernel (k = n = 10 against 2^21 rows, HBM bound, permutation
+    folded into the loads).  Inputs resident on the device; each step's
+    output is the next step's input (168 MB intermediates, larger than L2)."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import workloads as W
+
+    D = 1024
+    T = ndt.TensorF64
+    ts = [T.from_numpy(x) for x in W.cfg3_tensors(D)]
+    for t in ts:
+        t.device_ptr()
+    L, psi, W1, W2, R = ts
+    rhs = [psi, W1, W2, R]
+    flops = W.cfg3_flops(D)
+
+    def chain(ev=None):
+        cur = L
+        for i, ((la, lb), b) in enumerate(zip(W.CFG3_STEPS, rhs)):
+            if ev:
+                ev[i][0].record()
+            cur = ndt.contract_gemm(cur, la, b, lb)
+            if ev:
+                ev[i][1].record()
+        return cur
+
+    for _ in range(3):
+        chain()
+    torch.cuda.synchronize()
+    reps = 10
+    step_ms = [[] for _ in range(4)]
+    tot = []
+    for _ in range(reps):
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(4)]
+        chain(ev)
+        torch.cuda.synchronize()
+        for i in range(4):
+            step_ms[i].append(ev[i][0].elapsed_time(ev[i][1]))
+        tot.append(ev[0][0].elapsed_time(ev[3][1]))
+    ms = [statistics.median(x) for x in step_ms]
+    chain_ms = statistics.median(tot)
+    skinny_bytes = 2 * (2 * D * D) * 10 * 8 + 100 * 8  # read 2D^2 x 10, write 2D^2 x 10, W
+    out = {"workload": "DMRG environment chain L[1024,5,1024].psi[1024,2,2,1024].W1.W2.R[1024,5,1024] f64, "
+                       "contract_gemm x4",
+           "value": sum(flops) / (chain_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": chain_ms, "flop": sum(flops),
+           "steps": []}
+    for i in range(4):
+        st = {"step": i + 1, "ms": ms[i], "flop": flops[i], "tflops": flops[i] / (ms[i] * 1e-3) / 1e12}
+        if i in (1, 2):
+            gbs = skinny_bytes / (ms[i] * 1e-3) / 1e9
+            st["kernel"] = "skinny_kernel (k=n=10, strided loads)"
+            st["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                              "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes": skinny_bytes}
+        else:
+            st["kernel"] = "dmma_gemm_kernel" + (" (+ gather pack of the permuted A)" if i == 3 else "")
+            st["roofline"] = fp64_roofline(st["tflops"])
+        out["steps"].append(st)
+    return [out]
 
 
 if __name__ == "__main__":

@@ -25,12 +25,8 @@ namespace ndt {
 
 namespace {
 
-struct Ax1 {
-  int64_t n, s;
-};
-struct AxK {
-  int64_t n, sa, sb;
-};
+using Ax1 = StridedAxis;
+using AxK = ContractedAxis;
 
 struct Merged {
   bool ok = true;
@@ -126,6 +122,7 @@ void strided_contract(DType dt, const void* A, const void* B, void* C, const std
   for (const Ax1& a : M) m *= a.n;
   for (const Ax1& a : N) n *= a.n;
   for (const AxK& a : K) k *= a.n;
+  if (skinny_contract(dt, A, B, C, M, N, K, s)) return;
   std::vector<Ax1> ka, kb;
   for (const AxK& a : K) {
     ka.push_back({a.n, a.sa});

@@ -166,6 +166,25 @@ struct GemmOperand {
 void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand B, void* C,
           int64_t ldc, bool accumulate, cudaStream_t s);
 
+// Strided views used by the contraction driver: an axis of one operand
+// (extent, element stride) and a contracted axis pair (extent, stride in A,
+// stride in B).  Lists are ordered fastest first.
+struct StridedAxis {
+  int64_t n, s;
+};
+struct ContractedAxis {
+  int64_t n, sa, sb;
+};
+
+// Skinny contraction (skinny.cu): C[M..., N...] (dense, M fastest) =
+// sum_K A B when K and one of M / N are short (at most kSkinnyMax elements
+// each) and the other is long.  It reads both operands through their strides
+// in one pass (no packing), so a permuted operand costs nothing extra.
+// Returns false, doing nothing, when the shape is outside its range.
+constexpr int kSkinnyMax = 32;
+bool skinny_contract(DType dt, const void* A, const void* B, void* C, const std::vector<StridedAxis>& M,
+                     const std::vector<StridedAxis>& N, const std::vector<ContractedAxis>& K, cudaStream_t s);
+
 // Grouped GEMM over a device-side table.  Each problem is one output block
 // C_p (m_p x n_p, column-major, packed) = sum over its segments s of
 // A_s (m_p x k_s) * B_s (k_s x n_p).  All operands of one call share the

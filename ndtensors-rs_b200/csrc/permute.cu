@@ -18,6 +18,9 @@
 //            with cp.async (no register staging) while the current one is
 //            written out; the odd shared-memory row pitch keeps both phases
 //            bank-conflict free.
+//   runs     the source's stride-1 axis is the destination's first axis:
+//            contiguous runs copied in 16-byte vectors, offsets decomposed
+//            once per 16 KB chunk.
 //   generic  anything else (broadcast / pinned axes without a stride-1
 //            source axis, short rows): one destination element per thread.
 #include <algorithm>
@@ -238,9 +241,84 @@ __global__ void copy8_kernel(const double* __restrict__ src, double* __restrict_
     dst[i] = src[i];
 }
 
+// Run copy: the destination's first axis is the source's stride-1 axis, so
+// the permute moves contiguous runs of `run_len` elements.  A work item is a
+// 16 KB chunk of one run; its source / destination offsets are decomposed
+// once per item over the outer axes, and each thread keeps four independent
+// 16-byte loads in flight (8-byte copies when a run is not 16-byte aligned).
+struct RunParams {
+  int nd;
+  int vec;
+  int64_t n[kMaxGen], ssrc[kMaxGen], sdst[kMaxGen];
+  int64_t run_bytes, chunks, items;
+};
+constexpr int kRunUnroll = 4;
+constexpr int64_t kRunChunk = (int64_t)kThreads * kRunUnroll * 16;
+
+__global__ void __launch_bounds__(kThreads) permute_runs_kernel(const char* __restrict__ src,
+                                                                char* __restrict__ dst, int es,
+                                                                const __grid_constant__ RunParams p) {
+  for (int64_t it = blockIdx.x; it < p.items; it += gridDim.x) {
+    int64_t r = it / p.chunks;
+    const int64_t b0 = (it - r * p.chunks) * kRunChunk;
+    int64_t so = 0, dso = 0;
+    for (int d = 0; d < p.nd; d++) {
+      const int64_t q = r / p.n[d];
+      const int64_t digit = r - q * p.n[d];
+      r = q;
+      so += digit * p.ssrc[d];
+      dso += digit * p.sdst[d];
+    }
+    const char* s = src + so * es;
+    char* o = dst + dso * es;
+    const int64_t b1 = min(b0 + kRunChunk, p.run_bytes);
+    if (p.vec) {
+      int4 v[kRunUnroll];
+#pragma unroll
+      for (int u = 0; u < kRunUnroll; u++) {
+        const int64_t b = b0 + ((int64_t)u * kThreads + threadIdx.x) * 16;
+        if (b < b1) v[u] = *reinterpret_cast<const int4*>(s + b);
+      }
+#pragma unroll
+      for (int u = 0; u < kRunUnroll; u++) {
+        const int64_t b = b0 + ((int64_t)u * kThreads + threadIdx.x) * 16;
+        if (b < b1) *reinterpret_cast<int4*>(o + b) = v[u];
+      }
+    } else {
+      for (int64_t b = b0 + threadIdx.x * 8; b < b1; b += kThreads * 8)
+        *reinterpret_cast<double*>(o + b) = *reinterpret_cast<const double*>(s + b);
+    }
+  }
+}
+
 struct Ax {
   int64_t n, ssrc, sdst;
 };
+
+void launch_runs(const void* src, void* dst, const std::vector<Ax>& ax, int es, cudaStream_t s,
+                 const DeviceCtx& c) {
+  RunParams p{};
+  if ((int)ax.size() - 1 > kMaxGen) throw Error(ErrKind::Panic, "rank too large for the gather kernel");
+  p.nd = (int)ax.size() - 1;
+  bool vec = ((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0) && (ax[0].n * es) % 16 == 0;
+  int64_t nruns = 1;
+  for (int i = 0; i < p.nd; i++) {
+    const Ax& a = ax[i + 1];
+    p.n[i] = a.n;
+    p.ssrc[i] = a.ssrc;
+    p.sdst[i] = a.sdst;
+    vec = vec && (a.ssrc * es) % 16 == 0 && (a.sdst * es) % 16 == 0;
+    nruns *= a.n;
+  }
+  p.vec = vec ? 1 : 0;
+  p.run_bytes = ax[0].n * es;
+  p.chunks = (p.run_bytes + kRunChunk - 1) / kRunChunk;
+  p.items = nruns * p.chunks;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.items, (int64_t)c.sm_count * 64));
+  permute_runs_kernel<<<grid, kThreads, 0, s>>>((const char*)src, (char*)dst, es, p);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+}
 
 int grid_for(int64_t work_items, int per_sm, const DeviceCtx& c) {
   int64_t g = std::min<int64_t>(work_items, (int64_t)c.sm_count * per_sm);
@@ -444,6 +522,11 @@ void gather(DType dt, const void* src, void* dst, const GatherDesc& g, cudaStrea
       a_in = (int)i;
       break;
     }
+  // runs: the destination's first axis is also the source's stride-1 axis
+  if (a_in == 0 && m[0].n * E >= 64) {
+    launch_runs(src, dst, m, E, s, c);
+    return;
+  }
   if (a_in > 0) {
     bool ok = false;
     if (E == 8)

@@ -49,7 +49,20 @@ SHAPES = [
     ((2, 2, 2, 2, 2, 2, 2, 2), (7, 0, 6, 1, 5, 2, 4, 3)),
     ((40, 50, 2), (0, 2, 1)),  # stride-1 axis stays first: row gather
     ((4, 9, 100), (1, 0, 2)),
+    # run copies (source stride-1 axis stays the destination's first axis)
+    ((9, 5, 7), (0, 2, 1)),            # 72-byte runs: 8-byte copies (c128: 16-byte)
+    ((64, 10, 33), (0, 2, 1)),         # 512-byte runs, 16-byte vectors
+    ((3000, 3, 2), (0, 2, 1)),         # runs longer than one 16 KB chunk (c128)
+    ((16, 2, 5, 2, 3), (0, 1, 4, 3, 2)),  # first two axes merge into one run
 ]
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+def test_permute_run_copy_full_size(gpu, oracle, cplx):
+    """The DMRG operand shape [1024, 10, 2048] with perm (0, 2, 1): 8 KB runs."""
+    rng = np.random.default_rng(31)
+    a = _rand(rng, (1024, 10, 256 if cplx else 2048), cplx)
+    _check(gpu, oracle, a, (0, 2, 1))
 
 
 @pytest.mark.parametrize("cplx", [False, True])

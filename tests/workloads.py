@@ -120,3 +120,38 @@ def flops_blocksparse(Asp, la, Bsp, lb, complex_: bool) -> float:
             n = np.prod([sb[j][d[j]] for j in ub]) if ub else 1
             tot += (8.0 if complex_ else 2.0) * m * n * k
     return tot
+
+
+# DMRG environment-update chain, bond D (1024 in the benchmark),
+# MPO bond 5, physical dimension 2.  Entries N(0,1)/sqrt(fan-in), the fan-in
+# being the product of the axes the tensor contracts in its step.
+CFG3_STEPS = [
+    # (A labels, B labels): T1 = L.psi, T2 = T1.W1, T3 = T2.W2, E = T3.R
+    ([1, 2, -1], [-1, 3, 4, 5]),
+    ([1, -1, -2, 3, 4], [-1, 5, -2, 6]),
+    ([1, -2, 3, -1, 4], [-1, 5, -2, 6]),
+    ([1, -1, 2, -2, 3], [4, -2, -1]),
+]
+
+
+def cfg3_tensors(bond: int = 1024, seed: int = 1003):
+    """L[D,5,D], psi[D,2,2,D], W1, W2 [5,5,2,2], R[D,5,D] (column-major numpy)."""
+    rng = np.random.default_rng(seed)
+    D = bond
+
+    def t(shape, fan_in):
+        return np.asfortranarray(rng.standard_normal(shape) / np.sqrt(fan_in))
+
+    L = t((D, 5, D), D)
+    psi = t((D, 2, 2, D), D)
+    W1 = t((5, 5, 2, 2), 10)
+    W2 = t((5, 5, 2, 2), 10)
+    R = t((D, 5, D), 5 * D)
+    return L, psi, W1, W2, R
+
+
+def cfg3_flops(bond: int = 1024) -> List[float]:
+    """Real flop (2mnk) of the four steps."""
+    D = bond
+    return [2.0 * (5 * D) * D * (4 * D), 2.0 * (2 * D * D) * 10 * 10, 2.0 * (2 * D * D) * 10 * 10,
+            2.0 * (4 * D) * (5 * D) * D]
