@@ -12,7 +12,7 @@
 //            spans a contiguous run of the source (G_in axes), Q a contiguous
 //            run of the destination (G_out axes), so both the global loads and
 //            the global stores are coalesced (512-byte runs).  The tile
-//            geometry is fixed at compile time (64 x 64 f64, 32 x 64 c128),
+//            geometry is fixed at compile time (128 x 64 f64, 32 x 64 c128),
 //            so no integer division runs per element.  CTAs are persistent
 //            and double-buffered: the next tile is copied global -> shared
 //            with cp.async (no register staging) while the current one is
@@ -47,8 +47,13 @@ struct ElemT;
 template <>
 struct ElemT<8> {
   using type = double;
-  static constexpr int TP = 64;  // tile extent along the source-contiguous run
-  static constexpr int TQ = 64;  // tile extent along the destination-contiguous run
+  // Tile extents along the source-contiguous run (TP: 1 KB source rows) and
+  // the destination-contiguous run (TQ).  Two 64 KB buffers give one CTA per
+  // SM; on a 16^6 tensor that is 13.8 tiles per CTA (a 1.2% tail), which
+  // measured 11% faster than 64 x 64 tiles at three CTAs per SM (9.2 tiles
+  // each, up to 8% tail).
+  static constexpr int TP = 128;
+  static constexpr int TQ = 64;
 };
 template <>
 struct ElemT<16> {
