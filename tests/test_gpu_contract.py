@@ -119,7 +119,11 @@ def test_mps_merge_full_size(gpu, oracle):
 
 @pytest.mark.parametrize("dtype", [0, 1])
 @pytest.mark.parametrize("ak,bk", [(0, 1), (1, 1), (0, 0), (1, 0)])
-@pytest.mark.parametrize("m,n,k", [(1, 1, 1), (17, 9, 31), (128, 128, 16), (300, 200, 100), (1024, 64, 7)])
+@pytest.mark.parametrize("m,n,k", [
+    (1, 1, 1), (17, 9, 31), (128, 128, 16), (300, 200, 100), (1024, 64, 7),
+    # multi-wave grids with partial last waves, odd k, a single k-step
+    (1024, 1024, 256), (1000, 700, 1000), (777, 555, 333), (2048, 2048, 8),
+])
 def test_raw_gemm(gpu, dtype, ak, bk, m, n, k):
     """ndt_b200_gemm_dev against numpy, all operand layouts, edge tiles."""
     import torch
