@@ -9,9 +9,15 @@ larger than the 126 MB L2).  Metric unit: GB/s of algorithmic traffic,
 independent replicas (one process per GPU, no collective on the data path);
 `value` is the sum over ranks.
 
-Also reported on the same line (`contraction`): the dense f64 MPS two-site
-merge A[256,4,256] x B[256,4,256] -> C[256,4,4,256] (FP64 tensor-core
-TFLOP/s), and the complex128 permute of the same 16^6 shape.
+Also reported on the same line (`contraction`), each with its roofline: the
+batched and complex128 permutes of the same 16^6 shape, the dense f64 MPS
+two-site merge A[256,4,256] x B[256,4,256] -> C[256,4,4,256], a 4096^3 GEMM,
+the DMRG environment chain at bond 1024 (per step), and the block-sparse
+U(1) rank-4 (half scale) and c128 two-site MPS contractions (sharded across
+ranks with --gpus N > 1, plus the NCCL gather).  At one GPU each contraction
+also carries a CPU baseline: the reference's TTGT / per-pair algorithm with
+MKL (through torch) standing in for faer's GEMM, at one thread and at all
+host threads.
 
 --impl reference times the reference's CPU algorithm for the same workload
 on the host cores (the C restatement of GenericBackend::permute_into,
@@ -187,6 +193,144 @@ def cpu_permute_time(threads, sample_tensors=1, seed=2002):
             t.join()
     dt = time.perf_counter() - t0
     return dt / sample_tensors
+
+
+def _blocks_as_mats(sizes, coords, data, split):
+    """Each stored block of a packed column-major block-sparse tensor as a
+    matrix (first `split` axes = rows), keyed by block coordinates."""
+    import numpy as np
+
+    out, off = {}, 0
+    for c in coords:
+        shp = [sizes[ax][b] for ax, b in enumerate(c)]
+        n = int(np.prod(shp))
+        r = int(np.prod(shp[:split]))
+        out[tuple(c)] = data[off:off + n].reshape((r, n // r), order="F")
+        off += n
+    return out
+
+
+def cpu_contraction_baselines():
+    """CPU times of the contraction workloads the way the reference computes
+    them: TTGT with faer's GEMM at Par::Seq (contract/gemm.rs:158, :215) and
+    the per-pair loop of contract_blocksparse (contract/blocksparse.rs:144-180).
+    faer is not available; MKL through torch stands in for its GEMM, at one
+    thread (the reference's setting) and at all host threads.  Each sample is
+    bounded to a few seconds of CPU work.  Returns {workload key: baseline}."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, str(ROOT / "tests"))
+    import workloads as W
+
+    ncores = os.cpu_count() or 1
+    out = {}
+
+    def rate(fn, flop, reps):
+        fn()
+        ts = []
+        for _ in range(reps):
+            t0 = time.perf_counter()
+            fn()
+            ts.append(time.perf_counter() - t0)
+        return flop / statistics.median(ts) / 1e12
+
+    def both(key, fn, flop, reps, sample):
+        res = {}
+        for th in (1, ncores):
+            torch.set_num_threads(th)
+            res[th] = rate(fn, flop, reps)
+        torch.set_num_threads(ncores)
+        out[key] = {"value": res[1], "unit": "TFLOP/s", "cores": 1, "kind": "port", "sample": sample,
+                    "all_threads": {"value": res[ncores], "cores": ncores}}
+
+    g = torch.Generator().manual_seed(7)
+    # MPS merge: one GEMM m = n = 1024, k = 256
+    a = torch.randn(1024, 256, dtype=torch.float64, generator=g)
+    b = torch.randn(256, 1024, dtype=torch.float64, generator=g)
+    both("mps_merge", lambda: torch.matmul(a, b), 2.0 * 1024 * 1024 * 256, 5,
+         "full workload: A[256,4,256] x B[256,4,256] as one MKL dgemm (faer stand-in)")
+    # square GEMM: a 2048^3 sample of the 4096^3 workload
+    a = torch.randn(2048, 2048, dtype=torch.float64, generator=g)
+    b = torch.randn(2048, 2048, dtype=torch.float64, generator=g)
+    both("gemm4096", lambda: torch.matmul(a, b), 2.0 * 2048 ** 3, 2, "2048^3 sample, MKL dgemm (faer stand-in)")
+    # DMRG chain at bond 1024, every step as einsum (TTGT on MKL)
+    L, psi, W1, W2, R = [torch.from_numpy(np.ascontiguousarray(x)) for x in W.cfg3_tensors(1024)]
+    eqs = ["awx,xpqb->awpqb", "awpqb,wvpr->aqbvr", "aqbvr,vuqt->abrut", "abrut,zub->artz"]
+
+    def chain():
+        cur = L
+        for eq, rhs in zip(eqs, [psi, W1, W2, R]):
+            cur = torch.einsum(eq, cur, rhs)
+        return cur
+
+    both("dmrg_chain", chain, sum(W.cfg3_flops(1024)), 1,
+         "full chain at bond 1024, torch.einsum per step (permute + MKL dgemm)")
+    # c128 two-site MPS chain (A.S).B over its 128 block pairs
+    (sa, ca, ad), (ss, cs_, sd), (sb, cb, bd) = W.cfg5_tensors()
+    Am = _blocks_as_mats(sa, ca, ad, 2)
+    Bm = _blocks_as_mats(sb, cb, bd, 1)
+    offs = np.concatenate([[0], np.cumsum(sa[2])])
+    Am = {c: torch.from_numpy(m * sd[offs[c[2]]:offs[c[2]] + m.shape[1]][None, :]) for c, m in Am.items()}
+    Bm = {c: torch.from_numpy(m) for c, m in Bm.items()}
+    pairs = [(ca_, cb_) for ca_ in ca for cb_ in cb if ca_[2] == cb_[0]]
+    flop5 = W.flops_blocksparse((sa, ca, None), [1, 2, -1], (sb, cb, None), [-1, 3, 4], True)
+    diag_t = torch.from_numpy(sd)
+
+    def bs5():
+        outb = {}
+        for c in ca:  # diagonal scale of A's last axis
+            m = Am[c]
+            _ = m * diag_t[offs[c[2]]:offs[c[2]] + m.shape[1]][None, :]
+        for x, y in pairs:
+            key = (x[0], x[1], y[1], y[2])
+            r = torch.matmul(Am[x], Bm[y])
+            if key in outb:
+                outb[key] += r
+            else:
+                outb[key] = r
+        return outb
+
+    both("bs_c128_mps", bs5, flop5, 1,
+         "full chain: diagonal scale + 128 block-pair zgemm (MKL, faer stand-in) with per-block accumulation")
+    # U(1) rank-4 half scale: a strided sample of the block pairs (~2e10 flop)
+    dims = W.cfg4_dims(2)
+    sizes, coords = W.cfg4_structure(dims)
+    cset = set(coords)
+    allp = []
+    for x in coords:
+        for y in coords:
+            if x[2] == y[0] and x[3] == y[1]:
+                allp.append((x, y, 2.0 * dims[x[0]] * dims[x[1]] * dims[x[2]] * dims[x[3]] * dims[y[2]] * dims[y[3]]))
+    total = sum(f for _, _, f in allp)
+    stride = max(1, int(total / 2e10))
+    sample = allp[::stride]
+    flop4 = sum(f for _, _, f in sample)
+    mats = {}
+    for x, y, _ in sample:
+        for c, split, tag in ((x, 2, "a"), (y, 2, "b")):
+            if (tag, c) not in mats:
+                r = dims[c[0]] * dims[c[1]]
+                k2 = dims[c[2]] * dims[c[3]]
+                mats[(tag, c)] = torch.randn(r, k2, dtype=torch.float64, generator=g)
+    assert all(c in cset for c in [p[0] for p in sample])
+
+    def bs4():
+        outb = {}
+        for x, y, _ in sample:
+            key = (x[0], x[1], y[2], y[3])
+            r = torch.matmul(mats[("a", x)], mats[("b", y)])
+            if key in outb:
+                outb[key] += r
+            else:
+                outb[key] = r
+        return outb
+
+    both("bs_u1_rank4", bs4, flop4, 1,
+         f"{len(sample)} of {len(allp)} block pairs ({flop4:.3g} of {total:.3g} flop, every {stride}th pair), "
+         "dgemm per pair (MKL, faer stand-in) with per-block accumulation")
+    torch.set_num_threads(ncores)
+    return out
 
 
 def run_reference(args, world, rank):
@@ -404,6 +548,15 @@ def main():
         extras += run_blocksparse(args, torch, ndt, world, rank, pg)
 
     # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
+    if rank == 0 and world == 1 and not args.no_extras:
+        cb = cpu_contraction_baselines()
+        keymap = [("contract A[256,4,256]", "mps_merge"), ("f64 GEMM 4096^3", "gemm4096"), ("DMRG", "dmrg_chain"),
+                  ("block-sparse c128 two-site MPS (A.S).B", "bs_c128_mps"), ("block-sparse U(1)", "bs_u1_rank4")]
+        for e in extras:
+            for prefix, key in keymap:
+                if e["workload"].startswith(prefix) and key in cb:
+                    e["cpu_baseline"] = cb[key]
+
     cpu = None
     if rank == 0 and world == 1:
         t_cpu = cpu_permute_time(1)
