@@ -544,7 +544,7 @@ def main():
         fp64_peak(stream)
         if world == 1:
             extras += run_extras(args, torch, lib, ndt, stream, peaks)
-            extras += run_dmrg(args, torch, ndt, peaks)
+        extras += run_dmrg(args, torch, ndt, peaks, world, rank, pg)
         extras += run_blocksparse(args, torch, ndt, world, rank, pg)
 
     # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
@@ -755,19 +755,27 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     return out
 
 
-def run_dmrg(args, torch, ndt, peaks):
+def run_dmrg(args, torch, ndt, peaks, world=1, rank=0, pg=None):
     """DMRG environment-update chain, bond 1024: T1 = L.psi, T2 = T1.W1,
     T3 = T2.W2, E = T3.R through contract_gemm (8.67e10 flop).  Steps 1 and 4
     are DMMA GEMMs (step 4 packs its permuted operand); steps 2 and 3 run on
     the skinny kernel (k = n = 10 against 2^21 rows, HBM bound, permutation
     folded into the loads).  Inputs resident on the device; each step's
-    output is the next step's input (168 MB intermediates, larger than L2)."""
+    output is the next step's input (168 MB intermediates, larger than L2).
+    With N ranks the chain is split along the free index a (axis 0 of L and
+    of every intermediate): rank r runs all four steps on L[a0:a1], no
+    collective (strong scaling, times are the max over ranks)."""
     sys.path.insert(0, str(ROOT / "tests"))
+    import numpy as np
     import workloads as W
 
     D = 1024
     T = ndt.TensorF64
-    ts = [T.from_numpy(x) for x in W.cfg3_tensors(D)]
+    host = list(W.cfg3_tensors(D))
+    if world > 1:
+        a0, a1 = rank * D // world, (rank + 1) * D // world
+        host[0] = np.asfortranarray(host[0][a0:a1])
+    ts = [T.from_numpy(x) for x in host]
     for t in ts:
         t.device_ptr()
     L, psi, W1, W2, R = ts
@@ -792,6 +800,9 @@ def run_dmrg(args, torch, ndt, peaks):
     tot = []
     for _ in range(reps):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(4)]
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
         chain(ev)
         torch.cuda.synchronize()
         for i in range(4):
@@ -799,21 +810,27 @@ def run_dmrg(args, torch, ndt, peaks):
         tot.append(ev[0][0].elapsed_time(ev[3][1]))
     ms = [statistics.median(x) for x in step_ms]
     chain_ms = statistics.median(tot)
+    if pg:  # max over ranks
+        t = torch.tensor(ms + [chain_ms], device="cuda")
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        vals = t.tolist()
+        ms, chain_ms = vals[:4], vals[4]
     skinny_bytes = 2 * (2 * D * D) * 10 * 8 + 100 * 8  # read 2D^2 x 10, write 2D^2 x 10, W
     out = {"workload": "DMRG environment chain L[1024,5,1024].psi[1024,2,2,1024].W1.W2.R[1024,5,1024] f64, "
-                       "contract_gemm x4",
+                       "contract_gemm x4" + (f", split along a over {world} ranks" if world > 1 else ""),
            "value": sum(flops) / (chain_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": chain_ms, "flop": sum(flops),
-           "steps": []}
+           "n_gpus": world, "scaling": "strong" if world > 1 else None, "steps": []}
     for i in range(4):
-        st = {"step": i + 1, "ms": ms[i], "flop": flops[i], "tflops": flops[i] / (ms[i] * 1e-3) / 1e12}
+        tf = flops[i] / (ms[i] * 1e-3) / 1e12
+        st = {"step": i + 1, "ms": ms[i], "flop": flops[i], "tflops": tf}
         if i in (1, 2):
-            gbs = skinny_bytes / (ms[i] * 1e-3) / 1e9
+            gbs = skinny_bytes / (ms[i] * 1e-3) / 1e9 / world
             st["kernel"] = "skinny_kernel (k=n=10, strided loads)"
-            st["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                              "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes": skinny_bytes}
+            st["roofline"] = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s per GPU",
+                              "frac": gbs / peaks["hbm_gbs"], "algorithmic_bytes": skinny_bytes / world}
         else:
-            st["kernel"] = "dmma_gemm_kernel" + (" (+ gather pack of the permuted A)" if i == 3 else "")
-            st["roofline"] = fp64_roofline(st["tflops"])
+            st["kernel"] = "dmma_gemm_kernel" + (" (+ run-copy pack of the permuted A)" if i == 3 else "")
+            st["roofline"] = fp64_roofline(tf / world)
         out["steps"].append(st)
     return [out]
 

@@ -123,3 +123,28 @@ def test_skinny_launches_one_kernel(gpu):
     gpu.synchronize()
     assert gpu.launch_count() - n0 == 1
     assert out.shape == (64, 2, 64, 5, 2)
+
+
+@pytest.mark.parametrize("nranks", [2, 4])
+def test_dmrg_chain_split_along_free_index(gpu, nranks):
+    """The multi-GPU split of the chain: rank r runs all four steps on its
+    slab L[a0:a1] of the free index a (axis 0 of L and of every intermediate,
+    never contracted), with no collective.  Each slab's result equals the
+    matching rows of the unsplit chain."""
+    D = 256
+    L, psi, W1, W2, R = cfg3_tensors(bond=D)
+    T = gpu.TensorF64
+    rhs = [T.from_numpy(x) for x in (psi, W1, W2, R)]
+
+    def chain(l0):
+        cur = T.from_numpy(l0)
+        for (la, lb), b in zip(CFG3_STEPS, rhs):
+            cur = gpu.contract_gemm(cur, la, b, lb)
+        return cur.to_numpy()
+
+    full = chain(L)
+    for r in range(nranks):
+        a0, a1 = r * D // nranks, (r + 1) * D // nranks
+        part = chain(np.asfortranarray(L[a0:a1]))
+        assert part.shape == (a1 - a0,) + full.shape[1:]
+        assert rel_fro(part, full[a0:a1]) <= RTOL
