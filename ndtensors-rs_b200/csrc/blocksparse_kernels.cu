@@ -68,26 +68,45 @@ __device__ __forceinline__ double2 mulc(double2 a, double2 s) {
   return make_double2(a.x * s.x - a.y * s.y, a.x * s.y + a.y * s.x);
 }
 
+// One output block of the diagonal scale, reduced to what the kernel reads:
+// source / output / diagonal offsets, the column length (product of all but
+// the last extent), the number of columns (last extent), the diagonal length
+// and the block's first global column.
+struct DiagCols {
+  int64_t src, out, diag, inner, ncols, ndiag, col0;
+};
+
+// One warp per output column j of a block: out[:, j] = a[:, j] * s[j] for
+// j < ndiag, zero beyond (a diagonal block shorter than the axis).  The
+// column is contiguous (column-major, last axis slowest), so the warp streams
+// it with coalesced loads; the block is found once per column.
 template <typename T>
-__global__ void diag_scale_kernel(const T* __restrict__ a, const T* __restrict__ s, T* out,
-                                  const int64_t* __restrict__ offs, const BsBlockDesc* __restrict__ blocks,
-                                  int nblocks, int64_t total) {
-  // out[offs[b] + e'] = a[src_off + e'] * s[diag_off + e' / inner] for e' < inner * nlast_valid,
-  // zero beyond; dense_base = source offset, dstride[0] = diag offset,
-  // shape[0] = inner (product of all but the last extent), shape[1] = last
-  // extent of the output block, shape[2] = diagonal length.
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
-    const int b = find_block(offs, nblocks, e);
-    const BsBlockDesc& d = blocks[b];
-    const int64_t r = e - offs[b];
-    const int64_t j = r / d.shape[0];
-    T v;
-    if (j < d.shape[2]) {
-      v = mulc(a[d.dense_base + r], s[d.dstride[0] + j]);
-    } else {
-      v = T{};
+__global__ void __launch_bounds__(kThreads) diag_scale_kernel(const T* __restrict__ a, const T* __restrict__ s,
+                                                              T* __restrict__ out, const DiagCols* __restrict__ blk,
+                                                              int nblocks, int64_t ncols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t nwarps = ((int64_t)gridDim.x * kThreads) >> 5;
+  for (int64_t c = ((int64_t)blockIdx.x * kThreads + threadIdx.x) >> 5; c < ncols; c += nwarps) {
+    int lo = 0, hi = nblocks - 1;  // largest b with col0 <= c
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (blk[mid].col0 <= c)
+        lo = mid;
+      else
+        hi = mid - 1;
     }
-    out[e] = v;
+    const DiagCols d = blk[lo];
+    const int64_t j = c - d.col0;
+    const T* src = a + d.src + j * d.inner;
+    T* dst = out + d.out + j * d.inner;
+    if (j < d.ndiag) {
+      const T sv = s[d.diag + j];
+#pragma unroll 4
+      for (int64_t i = lane; i < d.inner; i += 32) dst[i] = mulc(src[i], sv);
+    } else {
+#pragma unroll 4
+      for (int64_t i = lane; i < d.inner; i += 32) dst[i] = T{};
+    }
   }
 }
 
@@ -150,18 +169,31 @@ void diag_scatter(DType dt, const void* diag, void* out, const std::vector<int64
 void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const std::vector<int64_t>& offs,
                    const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s) {
   if (total <= 0 || blocks.empty()) return;
-  Tables t = upload(offs, blocks, s);
+  // blocks[b]: dense_base = source offset, dstride[0] = diagonal offset,
+  // shape[0] = column length, shape[1] = columns, shape[2] = diagonal length
+  std::vector<DiagCols> h(blocks.size());
+  int64_t ncols = 0;
+  for (size_t b = 0; b < blocks.size(); b++) {
+    const BsBlockDesc& d = blocks[b];
+    h[b] = DiagCols{d.dense_base, offs[b], d.dstride[0], d.shape[0], d.shape[1], d.shape[2], ncols};
+    ncols += d.shape[1];
+  }
+  DiagCols* dt_tab = nullptr;
+  const size_t bytes = h.size() * sizeof(DiagCols);
+  NDT_CUDA(cudaMallocAsync((void**)&dt_tab, bytes, s));
+  NDT_CUDA(cudaMemcpyAsync(dt_tab, h.data(), bytes, cudaMemcpyHostToDevice, s));
+  const DeviceCtx& c = ctx();
+  const int64_t want = (ncols * 32 + kThreads - 1) / kThreads;
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)c.sm_count * 8));
   if (dt == DType::F64)
-    diag_scale_kernel<double><<<grid_of(total), kThreads, 0, s>>>((const double*)a, (const double*)sdiag,
-                                                                  (double*)out, t.offs, t.blocks,
-                                                                  (int)blocks.size(), total);
+    diag_scale_kernel<double><<<grid, kThreads, 0, s>>>((const double*)a, (const double*)sdiag, (double*)out, dt_tab,
+                                                        (int)h.size(), ncols);
   else
-    diag_scale_kernel<double2><<<grid_of(total), kThreads, 0, s>>>((const double2*)a, (const double2*)sdiag,
-                                                                   (double2*)out, t.offs, t.blocks,
-                                                                   (int)blocks.size(), total);
+    diag_scale_kernel<double2><<<grid, kThreads, 0, s>>>((const double2*)a, (const double2*)sdiag, (double2*)out,
+                                                         dt_tab, (int)h.size(), ncols);
   count_launch();
   NDT_CUDA(cudaGetLastError());
-  NDT_CUDA(cudaFreeAsync(t.mem, s));
+  NDT_CUDA(cudaFreeAsync(dt_tab, s));
 }
 
 }  // namespace ndt

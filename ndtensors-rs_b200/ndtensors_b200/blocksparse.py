@@ -318,10 +318,12 @@ def allgather(shard, group=None):
     Blocks come out sorted, as contract_blocksparse orders them.
 
     Shards are contiguous ranges of the sorted output block list, so rank r's
-    packed data is the r-th contiguous range of the gathered data.  On NCCL
-    the data stays in HBM: each rank's range is broadcast from that rank
-    straight into its place in one device buffer (no padding, no host copy);
-    on gloo (CPU tests) the ranges go through host memory."""
+    packed data is the r-th contiguous range of the gathered data.  Two
+    collectives: the per-rank lengths, then one all_gather of every rank's
+    [packed data, block coordinates] padded to the longest (on NCCL all links
+    carry data at once and nothing leaves HBM but the coordinates); one
+    device concatenation puts the data in packed order.  On gloo (CPU tests)
+    the same steps run on host tensors."""
     import torch
     import torch.distributed as dist
 
@@ -332,41 +334,37 @@ def allgather(shard, group=None):
     nd = len(sizes)
     width = shard._width
     nelem = shard.nnz
-    meta = torch.tensor([len(coords), nelem], dtype=torch.int64, device=dev)
-    metas = [torch.zeros_like(meta) for _ in range(world)]
-    dist.all_gather(metas, meta, group=group)
-    counts = [(int(m[0]), int(m[1])) for m in metas]
-    nb_max = max(c[0] for c in counts)
-    c_t = torch.full((max(nb_max, 1), nd), -1, dtype=torch.int64, device=dev)
-    if coords:
-        c_t[: len(coords)] = torch.tensor(coords, dtype=torch.int64, device=dev)
-    cs = [torch.empty_like(c_t) for _ in range(world)]
-    dist.all_gather(cs, c_t, group=group)
-    all_coords = []
-    for r in range(world):
-        all_coords += [tuple(int(x) for x in row) for row in cs[r][: counts[r][0]].cpu().tolist()]
-    offs = [0]
-    for _, ne in counts:
-        offs.append(offs[-1] + ne * width)
-    rank = dist.get_rank(group)
-    full = torch.empty(max(offs[-1], 1), dtype=torch.float64, device=dev)
-    if nelem:
+    nval = nelem * width                      # doubles of packed data
+    ncrd = len(coords) * nd                   # int64 coordinates
+    meta = torch.tensor([nval, ncrd], dtype=torch.int64, device=dev)
+    metas = torch.empty(world * 2, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(metas, meta, group=group)
+    counts = metas.view(world, 2).tolist()
+    pad = max(max(v + c for v, c in counts), 1)
+    send = torch.empty(pad, dtype=torch.float64, device=dev)
+    if nval:
         if nccl:
             # the shard was written on the library's stream
-            check_status(get_lib().ndt_b200_synchronize(), "synchronize")
-            own = torch.as_tensor(_DeviceSpan(shard.device_ptr(), nelem * width), device=dev)
+            if get_lib().ndt_b200_get_stream() != torch.cuda.current_stream().cuda_stream:
+                check_status(get_lib().ndt_b200_synchronize(), "synchronize")
+            own = torch.as_tensor(_DeviceSpan(shard.device_ptr(), nval), device=dev)
         else:
             own = torch.from_numpy(np.ascontiguousarray(shard.to_numpy_data()).view(np.float64))
-        full[offs[rank]: offs[rank + 1]].copy_(own)
-    for r in range(world):
-        if offs[r + 1] > offs[r]:
-            src = dist.get_global_rank(group, r) if group is not None else r
-            dist.broadcast(full[offs[r]: offs[r + 1]], src=src, group=group)
+        send[:nval].copy_(own)
+    if ncrd:
+        send[nval: nval + ncrd].view(torch.int64).copy_(
+            torch.tensor([x for c in coords for x in c], dtype=torch.int64, device=dev))
+    recv = torch.empty(world * pad, dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(recv, send, group=group)
+    crd = torch.cat([recv[r * pad + v: r * pad + v + c] for r, (v, c) in enumerate(counts) if c])
+    flat_c = crd.view(torch.int64).tolist() if crd.numel() else []
+    all_coords = [tuple(flat_c[i: i + nd]) for i in range(0, len(flat_c), nd)]
+    parts = [recv[r * pad: r * pad + v] for r, (v, _) in enumerate(counts) if v]
+    data = torch.cat(parts) if parts else torch.empty(0, dtype=torch.float64, device=dev)
     if nccl:
         torch.cuda.current_stream().synchronize()
-        data = full[: offs[-1]]
         return type(shard).from_torch(sizes, all_coords, data.view(torch.complex128) if width == 2 else data)
-    flat = full[: offs[-1]].numpy()
+    flat = data.numpy()
     return type(shard).from_blocks(sizes, all_coords, flat.view(np.complex128) if width == 2 else flat)
 
 
