@@ -406,60 +406,69 @@ void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
     launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true>(a, grid, s);
 }
 
-// Tile configurations (chosen by a sweep on B200).  f64: 128x128x32 (8
-// warps, 3 stages) or 64x64x32 (4 warps, 3 stages, two CTAs per SM) for grids
-// that would otherwise leave SMs idle; c128: 64x128x16 / 32x64x16.
+// Tile classes, indexed by `cls`, with their steady-state rate relative to
+// the best class (measured on B200 with each class forced: dense 4096^3 and
+// 4096 x 4096 x 1024, the DMRG and MPS contractions, both block-sparse
+// workloads):
+//   f64   0: 64x64x32, 4 warps, two CTAs per SM        1.00
+//         1: 128x128x32, 8 warps, one CTA per SM       0.97
+//   c128  0: 64x64x16, 4 warps, two CTAs per SM        1.00 (35.6 TFLOP/s on 4096 x 4096 x 1024)
+//         1: 64x128x16, 8 warps, one CTA per SM        0.93
+//         2: 32x64x16, 2 warps                         0.85
+// Smaller tiles waste less on the ragged edges of small blocks and fill the
+// SMs with fewer tiles; the heuristic weighs that against the rate.
+struct TileClass {
+  int bm, bn, per_sm;
+  double rate;
+};
+const TileClass kF64Classes[] = {{64, 64, 2, 1.0}, {128, 128, 1, 0.97}};
+const TileClass kC128Classes[] = {{64, 64, 2, 1.0}, {64, 128, 1, 0.93}, {32, 64, 2, 0.85}};
+int nclasses(bool cplx) { return cplx ? 3 : 2; }
+const TileClass& tile_class(bool cplx, int cls) { return cplx ? kC128Classes[cls] : kF64Classes[cls]; }
+
 template <bool CPLX, bool AK, bool BKM, bool VEC>
-void launch(const KArgs& a, int grid, bool small, cudaStream_t s) {
+void launch(const KArgs& a, int grid, int cls, cudaStream_t s) {
   if constexpr (!CPLX) {
-    if (small)
-      launch_cfg<false, 64, 64, 32, 2, 2, 3, AK, BKM, VEC>(a, grid, s);
-    else
+    if (cls == 1)
       launch_cfg<false, 128, 128, 32, 2, 4, 3, AK, BKM, VEC>(a, grid, s);
-  } else {
-    if (small)
-      launch_cfg<true, 32, 64, 16, 1, 2, 3, AK, BKM, false>(a, grid, s);
     else
+      launch_cfg<false, 64, 64, 32, 2, 2, 3, AK, BKM, VEC>(a, grid, s);
+  } else {
+    if (cls == 2)
+      launch_cfg<true, 32, 64, 16, 1, 2, 3, AK, BKM, false>(a, grid, s);
+    else if (cls == 1)
       launch_cfg<true, 64, 128, 16, 2, 4, 3, AK, BKM, false>(a, grid, s);
+    else
+      launch_cfg<true, 64, 64, 16, 2, 2, 3, AK, BKM, false>(a, grid, s);
   }
 }
 
 template <bool CPLX>
-void dispatch(const KArgs& a, int grid, bool small, bool ak, bool bk, bool vec, cudaStream_t s) {
+void dispatch(const KArgs& a, int grid, int cls, bool ak, bool bk, bool vec, cudaStream_t s) {
   if (!CPLX && vec) {
     if (ak && bk)
-      launch<CPLX, true, true, true>(a, grid, small, s);
+      launch<CPLX, true, true, true>(a, grid, cls, s);
     else if (ak && !bk)
-      launch<CPLX, true, false, true>(a, grid, small, s);
+      launch<CPLX, true, false, true>(a, grid, cls, s);
     else if (!ak && bk)
-      launch<CPLX, false, true, true>(a, grid, small, s);
+      launch<CPLX, false, true, true>(a, grid, cls, s);
     else
-      launch<CPLX, false, false, true>(a, grid, small, s);
+      launch<CPLX, false, false, true>(a, grid, cls, s);
     return;
   }
   if (ak && bk)
-    launch<CPLX, true, true, false>(a, grid, small, s);
+    launch<CPLX, true, true, false>(a, grid, cls, s);
   else if (ak && !bk)
-    launch<CPLX, true, false, false>(a, grid, small, s);
+    launch<CPLX, true, false, false>(a, grid, cls, s);
   else if (!ak && bk)
-    launch<CPLX, false, true, false>(a, grid, small, s);
+    launch<CPLX, false, true, false>(a, grid, cls, s);
   else
-    launch<CPLX, false, false, false>(a, grid, small, s);
+    launch<CPLX, false, false, false>(a, grid, cls, s);
 }
 
 // 16-byte pair copies need 16-byte aligned operand bases and even element
 // offsets / leading dimensions.
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
-
-void tile_dims(bool cplx, bool small, int* bm, int* bn) {
-  if (!cplx) {
-    *bm = small ? 64 : 128;
-    *bn = small ? 64 : 128;
-  } else {
-    *bm = small ? 32 : 64;
-    *bn = small ? 64 : 128;
-  }
-}
 
 }  // namespace
 
@@ -468,21 +477,21 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   if (m <= 0 || n <= 0) return;
   const bool cplx = dt == DType::C128;
   const DeviceCtx& c = ctx();
-  // Pick the tile size that fills the SMs best (waves of one CTA per SM for
-  // the big tile, ~2 per SM for the small one).
-  auto waves_eff = [&](bool small) {
-    int bm, bn;
-    tile_dims(cplx, small, &bm, &bn);
+  // Pick the tile class with the best estimated rate: useful / padded work,
+  // times the filled fraction of the last wave, times the class's rate.
+  auto waves_eff = [&](int cl) {
+    const TileClass& tc = tile_class(cplx, cl);
+    const int bm = tc.bm, bn = tc.bn;
     double tiles = (double)((m + bm - 1) / bm) * (double)((n + bn - 1) / bn);
-    double slots = (double)c.sm_count * (small ? 2 : 1);
+    double slots = (double)c.sm_count * tc.per_sm;
     double waves = std::ceil(tiles / slots);
     double useful = (double)m * n / ((double)((m + bm - 1) / bm) * bm * ((n + bn - 1) / bn) * bn);
-    // small tiles re-read operands twice as often; weight them down a bit
-    return tiles / (waves * slots) * useful * (small ? 0.9 : 1.0);
+    return tiles / (waves * slots) * useful * tc.rate;
   };
-  bool small = waves_eff(true) > waves_eff(false);
-  int bm, bn;
-  tile_dims(cplx, small, &bm, &bn);
+  int cls = 0;
+  for (int cl = 1; cl < nclasses(cplx); cl++)
+    if (waves_eff(cl) > waves_eff(cls)) cls = cl;
+  const int bm = tile_class(cplx, cls).bm, bn = tile_class(cplx, cls).bn;
   KArgs a{};
   a.A = A.ptr;
   a.B = B.ptr;
@@ -500,9 +509,9 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   int grid = a.mtiles * a.ntiles_n;
   const bool vec = aligned16(A.ptr) && aligned16(B.ptr) && A.ld % 2 == 0 && B.ld % 2 == 0;
   if (cplx)
-    dispatch<true>(a, grid, small, A.kmajor, B.kmajor, false, s);
+    dispatch<true>(a, grid, cls, A.kmajor, B.kmajor, false, s);
   else
-    dispatch<false>(a, grid, small, A.kmajor, B.kmajor, vec, s);
+    dispatch<false>(a, grid, cls, A.kmajor, B.kmajor, vec, s);
 }
 
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
@@ -513,9 +522,9 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   const DeviceCtx& c = ctx();
   // Tile list: every (problem, tile) with its work (tile area x total k),
   // heaviest first so the tail of the launch is made of small tiles.
-  auto build = [&](bool small, std::vector<int4>& tiles, double* eff) {
-    int bm, bn;
-    tile_dims(cplx, small, &bm, &bn);
+  auto build = [&](int cl, std::vector<int4>& tiles, double* eff) {
+    const TileClass& tc = tile_class(cplx, cl);
+    const int bm = tc.bm, bn = tc.bn;
     std::vector<std::pair<double, int4>> w;
     double useful = 0, padded = 0;
     for (size_t p = 0; p < probs.size(); p++) {
@@ -531,16 +540,22 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
     std::stable_sort(w.begin(), w.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
     tiles.resize(w.size());
     for (size_t i = 0; i < w.size(); i++) tiles[i] = w[i].second;
-    double slots = (double)c.sm_count * (small ? 2 : 1);
+    double slots = (double)c.sm_count * tc.per_sm;
     double waves = std::ceil((double)tiles.size() / slots);
-    *eff = useful / padded * std::min(1.0, (double)tiles.size() / (waves * slots)) * (small ? 0.9 : 1.0);
+    *eff = useful / padded * std::min(1.0, (double)tiles.size() / (waves * slots)) * tc.rate;
   };
-  std::vector<int4> tb, ts;
-  double eb, es;
-  build(false, tb, &eb);
-  build(true, ts, &es);
-  bool small = es > eb;
-  std::vector<int4>& tiles = small ? ts : tb;
+  std::vector<int4> tiles, cand;
+  int cls = 0;
+  double best = -1;
+  for (int cl = 0; cl < nclasses(cplx); cl++) {
+    double e;
+    build(cl, cand, &e);
+    if (e > best) {
+      best = e;
+      cls = cl;
+      tiles.swap(cand);
+    }
+  }
   // Device-side tables: problems, segments, tiles (one allocation).
   size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment),
          bt = tiles.size() * sizeof(int4);
@@ -566,9 +581,9 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   for (const GroupedSegment& sg : segs)
     vec = vec && sg.a_off % 2 == 0 && sg.b_off % 2 == 0 && sg.lda % 2 == 0 && sg.ldb % 2 == 0;
   if (cplx)
-    dispatch<true>(a, grid, small, a_kmajor, b_kmajor, false, s);
+    dispatch<true>(a, grid, cls, a_kmajor, b_kmajor, false, s);
   else
-    dispatch<false>(a, grid, small, a_kmajor, b_kmajor, vec, s);
+    dispatch<false>(a, grid, cls, a_kmajor, b_kmajor, vec, s);
   NDT_CUDA(cudaFreeAsync(d, s));
 }
 
