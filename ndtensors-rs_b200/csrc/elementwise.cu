@@ -34,6 +34,38 @@ __global__ void scale_c128(const double2* a, double2* c, int64_t n, double re, d
   }
 }
 
+// Split-K sum: C[i + j*ldc] (+)= sum_s W[s][i + j*m], partials summed in
+// split order (deterministic).  T is double or double2.
+template <typename T>
+__global__ void splitk_reduce_kernel(const T* __restrict__ w, int nsplit, int64_t m, int64_t n, T* c, int64_t ldc,
+                                     int accumulate) {
+  const int64_t mn = m * n;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < mn; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t j = e / m, i = e - j * m;
+    T acc = w[e];
+    for (int s = 1; s < nsplit; s++) {
+      const T v = w[(int64_t)s * mn + e];
+      if constexpr (sizeof(T) == 16) {
+        acc.x += v.x;
+        acc.y += v.y;
+      } else {
+        acc += v;
+      }
+    }
+    T* p = c + i + j * ldc;
+    if (accumulate) {
+      const T o = *p;
+      if constexpr (sizeof(T) == 16) {
+        acc.x += o.x;
+        acc.y += o.y;
+      } else {
+        acc += o;
+      }
+    }
+    *p = acc;
+  }
+}
+
 int grid_of(int64_t n) {
   const DeviceCtx& c = ctx();
   int64_t g = (n + kThreads - 1) / kThreads;
@@ -66,6 +98,19 @@ void scale_device(DType dt, const void* a, void* c, size_t n, double re, double 
     scale_f64<<<grid_of(n), kThreads, 0, s>>>((const double*)a, (double*)c, (int64_t)n, re);
   else
     scale_c128<<<grid_of(n), kThreads, 0, s>>>((const double2*)a, (double2*)c, (int64_t)n, re, im);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+}
+
+void splitk_reduce(DType dt, const void* w, int nsplit, int64_t m, int64_t n, void* c, int64_t ldc, bool accumulate,
+                   cudaStream_t s) {
+  if (m <= 0 || n <= 0) return;
+  if (dt == DType::F64)
+    splitk_reduce_kernel<double><<<grid_of(m * n), kThreads, 0, s>>>((const double*)w, nsplit, m, n, (double*)c, ldc,
+                                                                     accumulate ? 1 : 0);
+  else
+    splitk_reduce_kernel<double2><<<grid_of(m * n), kThreads, 0, s>>>((const double2*)w, nsplit, m, n, (double2*)c,
+                                                                      ldc, accumulate ? 1 : 0);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }

@@ -492,6 +492,36 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   for (int cl = 1; cl < nclasses(cplx); cl++)
     if (waves_eff(cl) > waves_eff(cls)) cls = cl;
   const int bm = tile_class(cplx, cls).bm, bn = tile_class(cplx, cls).bn;
+  // Split-K: when the grid leaves much of its last wave idle and k is long,
+  // the k-range is cut into S pieces (multiples of 32, at least 16 k-steps of
+  // 32 each) computed as S problems of one grouped launch into a workspace,
+  // then summed in split order into C (deterministic).  The sum costs about
+  // 3% of the GEMM at these sizes.
+  {
+    const TileClass& tc = tile_class(cplx, cls);
+    const double tiles = (double)((m + bm - 1) / bm) * (double)((n + bn - 1) / bn);
+    const double slots = (double)c.sm_count * tc.per_sm;
+    auto fill = [&](int S) { return tiles * S / (std::ceil(tiles * S / slots) * slots) * (S > 1 ? 0.97 : 1.0); };
+    int S = 1;
+    for (int cand = 2; cand <= 4; cand++)
+      if (k / cand >= 16 * 32 && fill(cand) > fill(S) + 0.02) S = cand;
+    if (S > 1) {
+      std::vector<GroupedProblem> probs(S);
+      std::vector<GroupedSegment> segs(S);
+      const int64_t kc = (k / S + 31) / 32 * 32;
+      for (int sp = 0; sp < S; sp++) {
+        const int64_t k0 = sp * kc, k1 = std::min<int64_t>(k, k0 + kc);
+        probs[sp] = GroupedProblem{m, n, (int64_t)sp * m * n, sp, 1};
+        segs[sp] = GroupedSegment{A.kmajor ? k0 : k0 * A.ld, B.kmajor ? k0 : k0 * B.ld, k1 - k0, A.ld, B.ld, -1};
+      }
+      void* w = nullptr;
+      NDT_CUDA(cudaMallocAsync(&w, (size_t)S * m * n * esize(dt), s));
+      grouped_gemm(dt, A.ptr, B.ptr, w, A.kmajor, B.kmajor, probs, segs, nullptr, s);
+      splitk_reduce(dt, w, S, m, n, Cp, ldc, accumulate, s);
+      NDT_CUDA(cudaFreeAsync(w, s));
+      return;
+    }
+  }
   KArgs a{};
   a.A = A.ptr;
   a.B = B.ptr;

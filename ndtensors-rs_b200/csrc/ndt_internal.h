@@ -7,12 +7,20 @@
 //                    write) and the dense tensor value type
 //   capi_dense.cpp   ndt_tensor_f64_* (the reference's C ABI) and ndt_tensor_c64_*
 //   permute.cu       strided gather / permutedims kernels and their planner
-//   gemm.cu          FP64 tensor-core (DMMA) GEMM: dense and grouped, f64 and c128
+//   gemm.cu          FP64 tensor-core (DMMA) GEMM: dense (with split-K) and
+//                    grouped, f64 and c128
+//   skinny.cu        contractions with a short contracted and a short free
+//                    extent (strided operand reads, DMMA)
 //   contract.cpp     label planning (naive ABI semantics and TTGT semantics),
 //                    contraction driver, VJP / JVP compositions
-//   elementwise.cu   fill, add, diagonal scaling
+//   contract_noalloc.cu  the allocation-free contraction entry point
+//   elementwise.cu   fill, add, scale, split-K sums
 //   blocksparse.cpp  block-sparse and diag-block-sparse tensors, block-pair
-//                    table, grouped contraction, ABI exports
+//                    table, grouped contraction, sharding, ABI exports
+//   blocksparse_kernels.cu  block-sparse <-> dense maps, diagonal placement
+//                    and scaling
+//   fp64_peak.cu     FP64 tensor peak microbenchmark (its own library, for
+//                    the bench's roofline)
 #pragma once
 
 #include <cuda_runtime.h>
@@ -226,6 +234,10 @@ void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const 
 void fill_device(DType dt, void* p, size_t n, double re, double im, cudaStream_t s);
 void add_device(DType dt, const void* a, const void* b, void* c, size_t n, cudaStream_t s);
 void scale_device(DType dt, const void* a, void* c, size_t n, double re, double im, cudaStream_t s);
+// C[i + j*ldc] (+)= sum over s < nsplit of W[s][i + j*m] (split-K partials,
+// summed in split order).
+void splitk_reduce(DType dt, const void* w, int nsplit, int64_t m, int64_t n, void* c, int64_t ldc, bool accumulate,
+                   cudaStream_t s);
 
 // Contractions
 enum class ContractSemantics { Naive, Gemm };

@@ -123,6 +123,8 @@ def test_mps_merge_full_size(gpu, oracle):
     (1, 1, 1), (17, 9, 31), (128, 128, 16), (300, 200, 100), (1024, 64, 7),
     # multi-wave grids with partial last waves, odd k, a single k-step
     (1024, 1024, 256), (1000, 700, 1000), (777, 555, 333), (2048, 2048, 8),
+    # split-K (a 3.4-wave grid over a long k): equal and ragged k splits
+    (4096, 1024, 1024), (4000, 1000, 1500),
 ])
 def test_raw_gemm(gpu, dtype, ak, bk, m, n, k):
     """ndt_b200_gemm_dev against numpy, all operand layouts, edge tiles."""
