@@ -2,12 +2,13 @@
 
 The compute lives in libndtensors_capi.so (C++ / CUDA for sm_100a); this
 package binds its C ABI with ctypes and mirrors the reference's Python API
-(TensorF64, contract, contract_vjp, contract_jvp) plus complex128 and
-block-sparse tensors.
+(TensorF64, contract, contract_vjp, contract_jvp) plus complex128,
+block-sparse tensors and whole-network contraction (contract_network).
 """
 
 from . import blocksparse
 from ._lib import get_lib, last_error, lib_path
+from .network import contract_network
 from .ops import contract, contract_gemm, contract_jvp, contract_vjp
 from .tensor import NDTensorsError, StatusCode, TensorC64, TensorF64, check_status
 
@@ -40,6 +41,7 @@ __all__ = [
     "contract_gemm",
     "contract_vjp",
     "contract_jvp",
+    "contract_network",
     "NDTensorsError",
     "StatusCode",
     "check_status",

@@ -50,7 +50,7 @@ def _shape_arr(shape: Sequence[int]):
 
 
 class _DenseBase:
-    __slots__ = ("_ptr", "_lib")
+    __slots__ = ("_ptr", "_lib", "_shape")
     _prefix = ""
     _np_dtype = np.float64
     _width = 1  # doubles per element
@@ -58,6 +58,7 @@ class _DenseBase:
     def __init__(self, ptr: int) -> None:
         self._lib = get_lib()
         self._ptr = ptr
+        self._shape = None  # a handle's shape never changes: cached on first query
 
     def __del__(self) -> None:
         if getattr(self, "_ptr", None):
@@ -126,15 +127,19 @@ class _DenseBase:
 
     @property
     def ndim(self) -> int:
+        if self._shape is not None:
+            return len(self._shape)
         return int(self._f("ndim")(self._ptr))
 
     @property
     def shape(self) -> Tuple[int, ...]:
-        n = self.ndim
-        out = (ctypes.c_size_t * max(n, 1))()
-        st = self._f("shape")(self._ptr, out)
-        check_status(st, "shape")
-        return tuple(int(out[i]) for i in range(n))
+        if self._shape is None:
+            n = self.ndim
+            out = (ctypes.c_size_t * max(n, 1))()
+            st = self._f("shape")(self._ptr, out)
+            check_status(st, "shape")
+            self._shape = tuple(int(out[i]) for i in range(n))
+        return self._shape
 
     def __len__(self) -> int:
         return int(self._f("len")(self._ptr))
