@@ -83,6 +83,18 @@ void* dev_alloc(size_t bytes, int device) {
   return p;
 }
 
+void ensure_dynamic_smem(const void* func, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, size_t> done;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& have = done[{dev, func}];
+  if (bytes > have) {
+    NDT_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    have = bytes;
+  }
+}
+
 void dev_free(void* p, int device) {
   if (!p) return;
   DeviceCtx& c = ctx(device);

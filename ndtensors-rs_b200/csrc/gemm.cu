@@ -388,11 +388,7 @@ template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, 
 void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
   using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM>;
   auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED>;
-  static bool attr = false;
-  if (!attr) {
-    NDT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::smem_bytes));
-    attr = true;
-  }
+  ensure_dynamic_smem((const void*)kern, C::smem_bytes);
   kern<<<grid, C::kThreads, C::smem_bytes, s>>>(a);
   count_launch();
   NDT_CUDA(cudaGetLastError());

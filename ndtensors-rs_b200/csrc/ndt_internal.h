@@ -91,6 +91,11 @@ void dev_free(void* p, int device);
 void* pinned_alloc(size_t bytes, bool* pinned);
 void pinned_free(void* p, size_t bytes, bool pinned);
 void empty_caches();
+// Allow `func` (a __global__ function) up to `bytes` of dynamic shared
+// memory on the current device.  The attribute is per device and per
+// function, so it is set once for each (device, function) and raised when a
+// launch needs more.  Thread safe.
+void ensure_dynamic_smem(const void* func, size_t bytes);
 
 // ---------------------------------------------------------------- storage
 // One buffer of `len` elements.  The device buffer is authoritative once a

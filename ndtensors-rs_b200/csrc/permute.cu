@@ -445,11 +445,7 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
   tp.n_outer = no;
   tp.ntiles = ntiles;
   const size_t smem = 2 * (size_t)ElemT<E>::TQ * (ElemT<E>::TP + 1) * E;
-  static bool attr_done = false;
-  if (!attr_done) {
-    NDT_CUDA(cudaFuncSetAttribute(permute_tiled_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_done = true;
-  }
+  ensure_dynamic_smem((const void*)permute_tiled_kernel<E>, smem);
   int per_sm = 0;
   NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, permute_tiled_kernel<E>, kThreads, smem));
   per_sm = std::max(1, per_sm);

@@ -341,11 +341,7 @@ template <bool CPLX, int KS, int NT>
 void launch_sk(SkArgs a, cudaStream_t s) {
   auto kern = skinny_kernel<CPLX, KS, NT>;
   const size_t smem = (size_t)kStages * (a.k + 1) * pitch<CPLX>() * (CPLX ? 16 : 8);
-  static size_t attr = 0;  // largest dynamic shared memory enabled so far
-  if (smem > attr) {
-    NDT_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr = smem;
-  }
+  ensure_dynamic_smem((const void*)kern, smem);
   const DeviceCtx& c = ctx();
   int per_sm = 0;
   NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
