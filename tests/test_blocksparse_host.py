@@ -70,7 +70,7 @@ def max_block_flops(A, la, B, lb):
     return max(per.values())
 
 
-def _gather_worker(rank, world, port, q):
+def _gather_worker(rank, world, port, q, cplx=False):
     import sys
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
@@ -89,8 +89,14 @@ def _gather_worker(rank, world, port, q):
         lens = [8, 2, 12, 1]
         offs = np.cumsum([0] + lens)
         data = np.arange(offs[-1], dtype=float) * 1.5
-        lo, hi = (0, 2) if rank == 0 else (2, 4)  # contiguous shards of the sorted block list
-        shard = ndt.blocksparse.BlockSparseF64.from_blocks(sizes, all_coords[lo:hi], data[offs[lo]:offs[hi]])
+        if cplx:
+            data = data - 0.5j * data[::-1]
+        # contiguous shards of the sorted block list; with 3 ranks the middle
+        # one holds no block (more ranks than output blocks)
+        ranges = [(0, 2), (2, 4)] if world == 2 else [(0, 2), (2, 2), (2, 4)]
+        lo, hi = ranges[rank]
+        cls = ndt.blocksparse.BlockSparseC64 if cplx else ndt.blocksparse.BlockSparseF64
+        shard = cls.from_blocks(sizes, all_coords[lo:hi], data[offs[lo]:offs[hi]])
         full = ndt.blocksparse.allgather(shard)
         ok = full.coords == all_coords and np.array_equal(full.to_numpy_data(), data)
         q.put((rank, bool(ok)))
@@ -98,7 +104,8 @@ def _gather_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_allgather_shards_gloo():
+@pytest.mark.parametrize("world,cplx", [(2, False), (3, True)])
+def test_allgather_shards_gloo(world, cplx):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -107,10 +114,10 @@ def test_allgather_shards_gloo():
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    ps = [ctx.Process(target=_gather_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_gather_worker, args=(r, world, port, q, cplx)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=120) for _ in ps]
     for p in ps:
         p.join(timeout=60)
-    assert sorted(res) == [(0, True), (1, True)]
+    assert sorted(res) == [(r, True) for r in range(world)]

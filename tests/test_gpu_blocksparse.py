@@ -210,3 +210,33 @@ def test_cfg5_reduced_bond_chain_vs_oracle(gpu, oracle):
     assert st == 0
     assert C.coords == Cr.coords and C.block_sizes == Cr.block_sizes
     assert rel_fro(C.to_numpy_data(), Cr.data) <= RTOL
+
+
+def test_shards_with_more_ranks_than_output_blocks(gpu):
+    """Eight ranks over three output blocks: five shards are empty, the rest
+    hold contiguous ranges, and together they are the full result."""
+    bs = gpu.blocksparse
+    rng = np.random.default_rng(41)
+    sizes = [[3, 4, 5], [2, 6]]
+    ca = [(0, 0), (1, 1), (2, 0)]
+    cb = [(0, 0), (1, 1)]
+    A = bs.BlockSparseF64.from_blocks(sizes, ca, rng.standard_normal(3 * 2 + 4 * 6 + 5 * 2))
+    B = bs.BlockSparseF64.from_blocks([[2, 6], [4, 3]], cb, rng.standard_normal(2 * 4 + 6 * 3))
+    full = bs.contract(A, [1, -1], B, [-1, 2])
+    shards = [bs.contract_shard(A, [1, -1], B, [-1, 2], r, 8) for r in range(8)]
+    assert sum(s.nnzblocks for s in shards) == full.nnzblocks == 3
+    assert sum(1 for s in shards if s.nnzblocks == 0) == 5
+    coords = [c for s in shards for c in s.coords]
+    assert coords == full.coords
+    data = np.concatenate([s.to_numpy_data() for s in shards])
+    np.testing.assert_array_equal(data, full.to_numpy_data())
+    blocks, flops = bs.shard_plan(A, [1, -1], B, [-1, 2], 8)
+    assert blocks == [s.nnzblocks for s in shards]
+
+
+@pytest.mark.parametrize("rank,nranks", [(-1, 2), (2, 2), (0, 0)])
+def test_shard_rejects_bad_rank(gpu, rank, nranks):
+    bs = gpu.blocksparse
+    A = bs.BlockSparseF64.from_blocks([[2], [3]], [(0, 0)], np.ones(6))
+    with pytest.raises(gpu.NDTensorsError):
+        bs.contract_shard(A, [1, -1], A, [2, -1], rank, nranks)
