@@ -206,6 +206,17 @@ ndt_blocksparse_f64* ndt_blocksparse_f64_contract_shard(const ndt_blocksparse_f6
                                                         size_t ndim_a, const ndt_blocksparse_f64* b,
                                                         const long* labels_b, size_t ndim_b, int rank, int nranks,
                                                         int* status);
+/* The listed output blocks only (coords: nout x output rank, natural order A-free ++ B-free), from
+   whatever blocks the operands hold.  A rank of a sharded contraction whose operands carry only the
+   blocks its output blocks reference computes its share this way.  No counterpart in the reference. */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_select(const ndt_blocksparse_f64* a, const long* labels_a,
+                                                         size_t ndim_a, const ndt_blocksparse_f64* b,
+                                                         const long* labels_b, size_t ndim_b,
+                                                         const size_t* out_coords, size_t nout, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_select(const ndt_blocksparse_c64* a, const long* labels_a,
+                                                         size_t ndim_a, const ndt_blocksparse_c64* b,
+                                                         const long* labels_b, size_t ndim_b,
+                                                         const size_t* out_coords, size_t nout, int* status);
 /* Host-only plan of contract_shard: output blocks and real flops per rank (either array may be NULL) */
 int ndt_blocksparse_f64_shard_plan(const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a,
                                    const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b, int nranks,

@@ -19,6 +19,7 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
+#include <set>
 #include <unordered_map>
 
 #include "../../include/ndtensors_capi.h"
@@ -144,8 +145,12 @@ struct ShardPlan {
   std::vector<double> flops;   // real flop per rank
 };
 
+// `select` (nsel output coordinates of rank |ua| + |ub|, natural order):
+// compute only those output blocks (the ones the pairs produce), e.g. one
+// rank's share when its operands hold only the blocks that share references.
 BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
-                         const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr) {
+                         const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
+                         const size_t* select = nullptr, size_t nsel = 0) {
   const size_t na = A.ndim(), nb = B.ndim();
   if (A.dt != B.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
   if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
@@ -196,6 +201,17 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
       for (size_t j : ub) oc.push_back(B.coords[b][j]);
       if (oc.empty()) oc.push_back(0);
       contrib[oc].push_back({a, b});
+    }
+  }
+  if (select) {
+    const size_t r = std::max<size_t>(ua.size() + ub.size(), 1);
+    std::set<std::vector<size_t>> want;
+    for (size_t i = 0; i < nsel; i++) want.insert(std::vector<size_t>(select + i * r, select + (i + 1) * r));
+    for (auto it = contrib.begin(); it != contrib.end();) {
+      if (want.count(it->first))
+        ++it;
+      else
+        it = contrib.erase(it);
     }
   }
   // TTGT of each pair is contract_gemm on the blocks (gemm.rs:47-236):
@@ -861,6 +877,19 @@ extern "C" {
     return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
       return new NdtBs{                                                                                              \
           bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), rank, nranks)};    \
+    });                                                                                                              \
+  }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_contract_select(const T* a, const long* la, size_t na, const T* b, const long* lb,       \
+                                            size_t nb, const size_t* out_coords, size_t nout, int* status) {        \
+    if (!status) return nullptr;                                                                                     \
+    if (!a || !b || (!la && na) || (!lb && nb) || (!out_coords && nout)) {                                          \
+      *status = NDT_INVALID_ARGUMENT;                                                                                \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
+      static const size_t none = 0;                                                                                  \
+      return new NdtBs{bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), 0,  \
+                                   1, nullptr, nout ? out_coords : &none, nout)};                                    \
     });                                                                                                              \
   }                                                                                                                  \
   T* ndt_blocksparse_##DT##_permutedims(const T* a, const size_t* perm, size_t nperm, int* status) {                 \

@@ -116,6 +116,8 @@ SIGNATURES = [
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
             (f"ndt_blocksparse_{dt}_contract_shard", vp,
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_int, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_select", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_size_p, ctypes.c_size_t, c_int_p]),
             (f"ndt_blocksparse_{dt}_shard_plan", ctypes.c_int,
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, ctypes.c_int, c_size_p,
               ctypes.POINTER(ctypes.c_double)]),

@@ -293,6 +293,19 @@ def contract_shard(a, labels_a, b, labels_b, rank: int, nranks: int):
     return type(a)(p)
 
 
+def contract_select(a, labels_a, b, labels_b, out_coords):
+    """Only the listed output blocks (natural order: A's free axes, then B's),
+    computed from the blocks the operands hold."""
+    la, na = _labels(labels_a)
+    lb, nb = _labels(labels_b)
+    flat = [int(x) for c in out_coords for x in c]
+    cs = (SZ * max(len(flat), 1))(*flat)
+    st = ctypes.c_int(-999)
+    p = a._f("contract_select")(a._ptr, la, na, b._ptr, lb, nb, cs, len(out_coords), ctypes.byref(st))
+    _raise(st.value, "blocksparse contract_select")
+    return type(a)(p)
+
+
 def shard_plan(a, labels_a, b, labels_b, nranks: int):
     """Output blocks and real flops per rank of contract_shard (host only)."""
     la, na = _labels(labels_a)
@@ -379,4 +392,4 @@ def contract_diag(a, labels_a, s, labels_s):
 
 
 __all__ = ["BlockSparseF64", "BlockSparseC64", "DiagBlockSparseF64", "DiagBlockSparseC64", "contract",
-           "contract_shard", "contract_diag"]
+           "contract_shard", "contract_select", "shard_plan", "allgather", "contract_diag"]

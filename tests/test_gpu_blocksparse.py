@@ -240,3 +240,31 @@ def test_shard_rejects_bad_rank(gpu, rank, nranks):
     A = bs.BlockSparseF64.from_blocks([[2], [3]], [(0, 0)], np.ones(6))
     with pytest.raises(gpu.NDTensorsError):
         bs.contract_shard(A, [1, -1], A, [2, -1], rank, nranks)
+
+
+def test_contract_select_from_referenced_blocks_only(gpu):
+    """A share of the U(1) rank-4 contraction computed from operands that hold
+    only the blocks its output blocks reference (what a rank of the literal
+    8-GPU run keeps) equals those blocks of the full contraction."""
+    bs = gpu.blocksparse
+    (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
+    A = bs.BlockSparseF64.from_blocks(sa, ca, a)
+    B = bs.BlockSparseF64.from_blocks(sb, cb, b)
+    full = bs.contract(A, la, B, lb)
+    outs = full.coords[3::4]
+    want = set(outs)
+    used_a = {x for x in ca for y in cb if x[2:] == y[:2] and (x[0], x[1], y[2], y[3]) in want}
+    used_b = {y for x in ca for y in cb if x[2:] == y[:2] and (x[0], x[1], y[2], y[3]) in want}
+
+    def sub(sizes, coords, data, keep):
+        offs = np.cumsum([0] + [int(np.prod([sizes[ax][c] for ax, c in enumerate(cc)])) for cc in coords])
+        kc = [c for c in coords if c in keep]
+        kd = np.concatenate([data[offs[i]:offs[i + 1]] for i, c in enumerate(coords) if c in keep])
+        return bs.BlockSparseF64.from_blocks(sizes, kc, kd)
+
+    As, Bs = sub(sa, ca, a, used_a), sub(sb, cb, b, used_b)
+    assert As.nnzblocks < A.nnzblocks
+    got = bs.contract_select(As, la, Bs, lb, outs + [(0, 0, 0, 8)])  # a coordinate no pair produces: ignored
+    assert got.coords == sorted(outs)
+    for c in outs:
+        np.testing.assert_allclose(got.block(c), full.block(c), rtol=1e-12, atol=1e-12)
