@@ -684,11 +684,13 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
 def literal_u1_rank4(torch, ndt, W, world, rank, timed):
     """configs[3] at its literal size: 489 blocks per operand, 68 GB per
     operand, 6.39e14 flop.  A+B+C do not fit one GPU; each rank keeps only the
-    A and B blocks its output blocks reference (104 GB at 4 ranks, 85 GB at
-    8) and computes its FLOP-balanced contiguous range of the sorted output
-    blocks with contract_select.  Block data: N(0,1) from a generator seeded
-    by (operand, block index), so a block shared by several ranks holds the
-    same values on all of them."""
+    A and B blocks its output blocks reference and computes its output blocks
+    with contract_select.  Output blocks go to ranks by longest processing
+    time (balanced FLOPs; 105 GB per rank at 8 ranks) when every rank's
+    referenced blocks fit in 65% of the device memory, else as the
+    contiguous FLOP-balanced ranges of contract_shard (104 GB per rank at 4).
+    Block data: N(0,1) from a generator seeded by (operand, block index), so
+    a block shared by several ranks holds the same values on all of them."""
     from math import prod
 
     bs = ndt.blocksparse
@@ -703,15 +705,34 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
                 pairs.setdefault((x[0], x[1], y[2], y[3]), []).append(
                     (x, y, 2.0 * elems[x] * dims[y[2]] * dims[y[3]]))
     outs = sorted(pairs)
-    work = [sum(f for _, _, f in pairs[o]) for o in outs]
-    total = sum(work)
-    cut, acc, r = [0] + [len(outs)] * world, 0.0, 1  # the library's cut rule
-    for i, w in enumerate(work):
-        acc += w
-        while r < world and acc >= total * r / world:
-            cut[r] = i + 1
+    work = {o: sum(f for _, _, f in pairs[o]) for o in outs}
+    total = sum(work.values())
+
+    def footprint(lst):  # bytes of referenced A, B blocks and output blocks
+        a = {x for o in lst for x, _, _ in pairs[o]}
+        b = {y for o in lst for _, y, _ in pairs[o]}
+        return 8 * (sum(elems[c] for c in a) + sum(elems[c] for c in b) + sum(elems[o] for o in lst))
+
+    # contiguous FLOP-balanced ranges of the sorted output blocks (the
+    # library's contract_shard rule): small footprints, coarse balance
+    contiguous, acc, r = [[] for _ in range(world)], 0.0, 0
+    for o in outs:
+        while r < world - 1 and acc >= total * (r + 1) / world:
             r += 1
-    mine = outs[cut[rank]:cut[rank + 1]]
+        contiguous[r].append(o)
+        acc += work[o]
+    # longest-processing-time assignment: balanced FLOPs, larger footprints;
+    # used when every rank's blocks fit in 65% of the device memory
+    lpt = [[] for _ in range(world)]
+    load = [0.0] * world
+    for o in sorted(outs, key=lambda o: -work[o]):
+        q = min(range(world), key=lambda i: load[i])
+        lpt[q].append(o)
+        load[q] += work[o]
+    budget = 0.65 * torch.cuda.mem_get_info()[1]
+    use_lpt = max(footprint(lst) for lst in lpt) <= budget
+    plan = lpt if use_lpt else contiguous
+    mine = sorted(plan[rank])
     used_a = {x for o in mine for x, _, _ in pairs[o]}
     used_b = {y for o in mine for _, y, _ in pairs[o]}
 
@@ -737,7 +758,9 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
                         "output blocks reference",
             "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": total, "n_gpus": world, "scaling": "strong",
             "roofline": fp64_roofline(tf / world),
-            "max_rank_flop_share": max(sum(work[cut[q]:cut[q + 1]]) for q in range(world)) / total}
+            "assignment": "longest-processing-time" if use_lpt else "contiguous FLOP-balanced ranges",
+            "max_rank_flop_share": max(sum(work[o] for o in lst) for lst in plan) / total,
+            "max_rank_gb": max(footprint(lst) for lst in plan) / 1e9}
 
 
 def run_extras(args, torch, lib, ndt, stream, peaks):

@@ -268,3 +268,42 @@ def test_contract_select_from_referenced_blocks_only(gpu):
     assert got.coords == sorted(outs)
     for c in outs:
         np.testing.assert_allclose(got.block(c), full.block(c), rtol=1e-12, atol=1e-12)
+
+
+def test_literal_size_selected_blocks_vs_numpy(gpu):
+    """The literal U(1) rank-4 structure (sector dims [8,24,56,96,144,96,56,24,8],
+    68 GB per operand): the twelve output blocks that need the fewest input
+    elements, computed with contract_select from operands holding only their
+    referenced blocks, against numpy (2-pair outputs included)."""
+    from math import prod
+
+    from workloads import cfg4_dims, cfg4_structure
+
+    bs = gpu.blocksparse
+    dims = cfg4_dims(1)
+    sizes, coords = cfg4_structure(dims)
+    el = {c: prod(dims[x] for x in c) for c in coords}
+    pairs = {}
+    for x in coords:
+        for y in coords:
+            if x[2:] == y[:2]:
+                pairs.setdefault((x[0], x[1], y[2], y[3]), []).append((x, y))
+    cost = {o: sum(el[c] for c in {p[0] for p in ps} | {p[1] for p in ps}) for o, ps in pairs.items()}
+    outs = sorted(sorted(pairs, key=lambda o: (cost[o], o))[:12])
+    need_a = [c for c in coords if any(c == p[0] for o in outs for p in pairs[o])]
+    need_b = [c for c in coords if any(c == p[1] for o in outs for p in pairs[o])]
+    rng = np.random.default_rng(43)
+    da = {c: rng.standard_normal(el[c]) for c in need_a}
+    db = {c: rng.standard_normal(el[c]) for c in need_b}
+    A = bs.BlockSparseF64.from_blocks(sizes, need_a, np.concatenate([da[c] for c in need_a]))
+    B = bs.BlockSparseF64.from_blocks(sizes, need_b, np.concatenate([db[c] for c in need_b]))
+    got = bs.contract_select(A, [1, 2, -1, -2], B, [-1, -2, 3, 4], outs)
+    assert got.coords == outs
+    for o in outs:
+        m, n = dims[o[0]] * dims[o[1]], dims[o[2]] * dims[o[3]]
+        ref = np.zeros((m, n))
+        for x, y in pairs[o]:
+            k = dims[x[2]] * dims[x[3]]
+            ref += da[x].reshape((m, k), order="F") @ db[y].reshape((k, n), order="F")
+        blk = got.block(o).reshape((m, n), order="F")
+        assert np.linalg.norm(blk - ref) <= 1e-12 * np.linalg.norm(ref)
