@@ -250,6 +250,20 @@ def cpu_contraction_baselines():
     b = torch.randn(256, 1024, dtype=torch.float64, generator=g)
     both("mps_merge", lambda: torch.matmul(a, b), 2.0 * 1024 * 1024 * 256, 5,
          "full workload: A[256,4,256] x B[256,4,256] as one MKL dgemm (faer stand-in)")
+    # the reference's C-ABI contract is the naive loop (naive.rs:45-187), far
+    # too slow at this size: timed through the oracle's restatement of it on
+    # the same pattern scaled down (A[48,4,48] x B[48,4,48]), one thread
+    from oracle import oracle as orc
+
+    rng = np.random.default_rng(5)
+    na, nb = rng.standard_normal((48, 4, 48)), rng.standard_normal((48, 4, 48))
+    orc.contract_naive(na, [1, 2, -1], nb, [-1, 3, 4])
+    t0 = time.perf_counter()
+    orc.contract_naive(na, [1, 2, -1], nb, [-1, 3, 4])
+    naive_s = time.perf_counter() - t0
+    out["mps_merge"]["abi_naive_contract"] = {
+        "value": 2.0 * 192 * 192 * 48 / naive_s / 1e12, "unit": "TFLOP/s", "cores": 1, "kind": "port",
+        "sample": "A[48,4,48] x B[48,4,48] through the oracle's restatement of naive.rs (the C ABI's contract)"}
     # square GEMM: a 2048^3 sample of the 4096^3 workload
     a = torch.randn(2048, 2048, dtype=torch.float64, generator=g)
     b = torch.randn(2048, 2048, dtype=torch.float64, generator=g)
