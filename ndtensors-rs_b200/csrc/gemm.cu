@@ -112,6 +112,8 @@ struct CopyPlan {
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
           bool GROUPED>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(const __grid_constant__ KArgs args) {
+  pdl_release();
+  pdl_wait();  // before the first global access (tile tables, operands)
   using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM>;
   constexpr int NTH = C::kThreads, MT = C::MT, NT = C::NT, ES = C::ES;
   constexpr int LDA = C::PA::value, LDB = C::PB::value;
@@ -389,7 +391,7 @@ void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
   using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM>;
   auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED>;
   ensure_dynamic_smem((const void*)kern, C::smem_bytes);
-  kern<<<grid, C::kThreads, C::smem_bytes, s>>>(a);
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }

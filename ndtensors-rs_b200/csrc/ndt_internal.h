@@ -30,6 +30,7 @@
 #include <memory>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace ndt {
@@ -161,6 +162,29 @@ struct GatherDesc {
   std::vector<int64_t> src_strides; // in elements, per destination axis
 };
 void gather(DType dt, const void* src, void* dst, const GatherDesc& g, cudaStream_t s);
+// Programmatic dependent launch (sm_90+).  A kernel launched with
+// launch_pdl may be scheduled while the previous kernel on the stream is
+// still finishing, so launch latency and its own setup overlap that kernel's
+// tail.  Every kernel launched this way executes pdl_wait() before its first
+// global memory access (griddepcontrol.wait: the previous grid has completed
+// and its writes are visible), and pdl_release() early to let the next
+// kernel be scheduled the same way.
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+template <typename... KParams, typename... Args>
+void launch_pdl(void (*kern)(KParams...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NDT_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
 // Number of device kernels launched by this library since load (for benches).
 uint64_t launch_count();
 void count_launch();

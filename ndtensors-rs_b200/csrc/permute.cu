@@ -102,6 +102,12 @@ __global__ void __launch_bounds__(kThreads) permute_tiled_kernel(const typename 
   __shared__ int64_t tile_src[3], tile_dst[3];
   __shared__ int peff_s[3], qeff_s[3];
 
+  // Programmatic dependent launch: the next kernel on the stream may be
+  // scheduled as soon as this grid's CTAs start retiring (its setup overlaps
+  // this grid's tail), and this grid's own setup below overlaps the previous
+  // kernel; griddepcontrol.wait then holds every global access until the
+  // previous grid has completed and its writes are visible.
+  pdl_release();
   // In-tile offset tables, identical for every tile of the launch.
   for (int q = threadIdx.x; q < TQ; q += blockDim.x) {
     int64_t off = 0;
@@ -180,6 +186,7 @@ __global__ void __launch_bounds__(kThreads) permute_tiled_kernel(const typename 
   // last reader, a buffer one barrier after.
   int64_t t = blockIdx.x;
   if (threadIdx.x == 0 && t < tp.ntiles) bases(t, 0);
+  pdl_wait();
   __syncthreads();  // tables and slot 0 ready
   if (t < tp.ntiles) issue_reads(0, 0);
   asm volatile("cp.async.commit_group;\n" ::);
@@ -263,6 +270,8 @@ constexpr int64_t kRunChunk = (int64_t)kThreads * kRunUnroll * 16;
 __global__ void __launch_bounds__(kThreads) permute_runs_kernel(const char* __restrict__ src,
                                                                 char* __restrict__ dst, int es,
                                                                 const __grid_constant__ RunParams p) {
+  pdl_release();
+  pdl_wait();
   for (int64_t it = blockIdx.x; it < p.items; it += gridDim.x) {
     int64_t r = it / p.chunks;
     const int64_t b0 = (it - r * p.chunks) * kRunChunk;
@@ -320,7 +329,7 @@ void launch_runs(const void* src, void* dst, const std::vector<Ax>& ax, int es, 
   p.chunks = (p.run_bytes + kRunChunk - 1) / kRunChunk;
   p.items = nruns * p.chunks;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(p.items, (int64_t)c.sm_count * 64));
-  permute_runs_kernel<<<grid, kThreads, 0, s>>>((const char*)src, (char*)dst, es, p);
+  launch_pdl(permute_runs_kernel, dim3(grid), dim3(kThreads), 0, s, (const char*)src, (char*)dst, es, p);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }
@@ -451,7 +460,7 @@ void launch_tiled(const void* src, void* dst, const std::vector<Ax>& ax, int a_i
   per_sm = std::max(1, per_sm);
   int grid = grid_for(ntiles, per_sm, c);
   using T = typename ElemT<E>::type;
-  permute_tiled_kernel<E><<<grid, kThreads, smem, s>>>((const T*)src, (T*)dst, tp);
+  launch_pdl(permute_tiled_kernel<E>, dim3(grid), dim3(kThreads), smem, s, (const T*)src, (T*)dst, tp);
   count_launch();
   NDT_CUDA(cudaGetLastError());
   *ok = true;

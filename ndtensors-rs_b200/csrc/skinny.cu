@@ -132,6 +132,8 @@ struct Elem<true> {
 // CTAs per SM, 24 warps to hide the copy and tensor latencies.
 template <bool CPLX, int KS, int NT>
 __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 1) skinny_kernel(const __grid_constant__ SkArgs a) {
+  pdl_release();
+  pdl_wait();  // before the first global access
   using T = typename Elem<CPLX>::T;
   constexpr int KP = KS * 8;
   constexpr int ES = sizeof(T);
@@ -347,7 +349,7 @@ void launch_sk(SkArgs a, cudaStream_t s) {
   NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
   a.ntiles = (a.rows + kTileRows - 1) / kTileRows;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(a.ntiles, (int64_t)c.sm_count * std::max(per_sm, 1)));
-  kern<<<grid, kThreads, smem, s>>>(a);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), smem, s, a);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }
