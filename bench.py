@@ -29,6 +29,7 @@ from __future__ import annotations
 import argparse
 import ctypes
 import json
+import math
 import os
 import statistics
 import sys
@@ -808,35 +809,78 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": gbs / peaks["hbm_gbs"], "traffic": ncu_traffic("permute_16p6_c128")}})
     del src, dst
-    # dense f64 MPS merge: A[256,4,256] x B[256,4,256] (labels (1,2,-1),(-1,3,4)) as one DMMA GEMM
+    # dense f64 MPS merge: A[256,4,256] x B[256,4,256] (labels (1,2,-1),(-1,3,4)) as one DMMA GEMM.
+    # Timed as a stream of NM independent merges on distinct operands (12 MB each, NM x 12 MB > L2),
+    # launched back to back between one event pair: a single launch between two events carries a
+    # fixed event / launch cost of several microseconds on this part, a fifth of this 20 us kernel.
     m, n, k = 1024, 1024, 256
-    A = torch.randn(m * k, dtype=torch.float64, device="cuda")
-    Bt = torch.randn(k * n, dtype=torch.float64, device="cuda")
-    Ct = torch.empty(m * n, dtype=torch.float64, device="cuda")
+    NM = 16
+    As = torch.randn(NM, m * k, dtype=torch.float64, device="cuda")
+    Bs = torch.randn(NM, k * n, dtype=torch.float64, device="cuda")
+    Cs = torch.empty(NM, m * n, dtype=torch.float64, device="cuda")
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.float64, device="cuda")
 
+    def g(i):
+        st = lib.ndt_b200_gemm_dev(0, m, n, k, ctypes.c_void_p(As[i].data_ptr()), m, 0,
+                                   ctypes.c_void_p(Bs[i].data_ptr()), k, 1, ctypes.c_void_p(Cs[i].data_ptr()), m, 0,
+                                   sptr)
+        assert st == 0
+
+    for i in range(NM):
+        g(i)
+    reps = 10
+    per = []
+    for _ in range(reps):
+        flush.zero_()  # L2 flush before each stream (outside the events)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(NM):
+            g(i)
+        b.record()
+        torch.cuda.synchronize()
+        per.append(a.elapsed_time(b) / NM)
+    t = statistics.mean(per)
+    single = []
+    for _ in range(20):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g(0)
+        b.record()
+        torch.cuda.synchronize()
+        single.append(a.elapsed_time(b))
+    # cuBLAS DGEMM (torch.matmul) on the same operands and layout, timed the same way
+    Am = [As[i].view(k, m).t() for i in range(NM)]
+    Bm = [Bs[i].view(n, k).t() for i in range(NM)]
+    for i in range(NM):
+        torch.matmul(Am[i], Bm[i])
+    lib_per = []
+    for _ in range(reps):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for i in range(NM):
+            torch.matmul(Am[i], Bm[i])
+        b.record()
+        torch.cuda.synchronize()
+        lib_per.append(a.elapsed_time(b) / NM)
+    tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
+    # 64x64 tiles of four 32x32 warp tiles; FP64 MMA throughput is per SM sub-partition (4 per SM)
+    tiles, parts = (m // 64) * (n // 64), torch.cuda.get_device_properties(0).multi_processor_count * 4
+    out.append({"workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
+                "value": tf, "unit": "TFLOP/s", "ms": t,
+                "timing": f"{NM} independent merges back to back per event pair, L2 flushed before each stream",
+                "single_launch_ms": statistics.mean(single),
+                "cublas_dgemm_ms": statistics.mean(lib_per),
+                "balance_ceiling": tiles * 4 / (math.ceil(tiles * 4 / parts) * parts),
+                "roofline": fp64_roofline(tf)})
+    del As, Bs, Cs, Am, Bm
+    # a large square f64 GEMM for the kernel's steady-state rate
     def g():
         st = lib.ndt_b200_gemm_dev(0, m, n, k, ctypes.c_void_p(A.data_ptr()), m, 0, ctypes.c_void_p(Bt.data_ptr()),
                                    k, 1, ctypes.c_void_p(Ct.data_ptr()), m, 0, sptr)
         assert st == 0
 
-    for _ in range(5):
-        g()
-    times = []
-    for _ in range(50):
-        flush.zero_()  # L2 flush between timed launches (outside the events)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        g()
-        b.record()
-        torch.cuda.synchronize()
-        times.append(a.elapsed_time(b))
-    t = statistics.mean(times)
-    tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
-    out.append({"workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
-                "value": tf, "unit": "TFLOP/s", "ms": t,
-                "roofline": fp64_roofline(tf)})
-    # a large square f64 GEMM for the kernel's steady-state rate
     m = n = k = 4096
     A = torch.randn(m * k, dtype=torch.float64, device="cuda")
     Bt = torch.randn(k * n, dtype=torch.float64, device="cuda")
