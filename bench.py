@@ -525,31 +525,76 @@ def main():
     hp = ctypes.cast(host_in.data_ptr(), ctypes.POINTER(ctypes.c_double))
     st = ctypes.c_int(-999)
 
-    def e2e_step():
+    dev_index = torch.cuda.current_device()
+
+    def e2e_steps_on_thread(count, errs):
+        # one host thread's share of the steps; ctypes releases the GIL inside each C call
+        torch.cuda.set_device(dev_index)
+        stl = ctypes.c_int(-999)
+        for _ in range(count):
+            t = lib.ndt_tensor_f64_from_data(hp, NELEM, shape_c, 6, ctypes.byref(stl))
+            p = lib.ndt_tensor_f64_permutedims(t, perm_c, 6, ctypes.byref(stl))
+            d = lib.ndt_tensor_f64_data(p)  # device -> host read of the result
+            if not d or stl.value != 0:
+                errs.append(stl.value)
+            lib.ndt_tensor_f64_release(p)
+            lib.ndt_tensor_f64_release(t)
+
+    def e2e_run(nsteps, nthreads):
+        """Wall time of nsteps H2D -> permutedims -> D2H steps through the C ABI,
+        split over nthreads host threads (the library uploads on one stream,
+        computes on another and reads back on a third, so one thread's read
+        overlaps another's upload on the two PCIe directions)."""
+        errs = []
+        share = [nsteps // nthreads + (1 if i < nsteps % nthreads else 0) for i in range(nthreads)]
+        ths = [threading.Thread(target=e2e_steps_on_thread, args=(c, errs)) for c in share]
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - w0
+        assert not errs, f"C ABI step failed: {errs[:3]}"
+        w = torch.tensor([dt], device="cuda")
+        if pg:
+            pg.all_reduce(w, op=pg.ReduceOp.MAX)
+        return float(w.item())
+
+    # the C ABI's host result equals the device reference, bit for bit
+    import numpy as np
+    t = lib.ndt_tensor_f64_from_data(hp, NELEM, shape_c, 6, ctypes.byref(st))
+    p = lib.ndt_tensor_f64_permutedims(t, perm_c, 6, ctypes.byref(st))
+    d = lib.ndt_tensor_f64_data(p)
+    assert d and st.value == 0 and np.array_equal(np.ctypeslib.as_array(d, shape=(NELEM,)),
+                                                  ref0.flatten().cpu().numpy()), "C ABI permute mismatch"
+    lib.ndt_tensor_f64_release(p)
+    lib.ndt_tensor_f64_release(t)
+    E2E_THREADS = 2
+    # warm-up: hold 2 x E2E_THREADS steps' tensors at once, so the library's pinned host
+    # mirrors and device pool already hold what the threads can have in flight, then run
+    # the threaded loop itself
+    held = []
+    for _ in range(2 * E2E_THREADS):
         t = lib.ndt_tensor_f64_from_data(hp, NELEM, shape_c, 6, ctypes.byref(st))
         p = lib.ndt_tensor_f64_permutedims(t, perm_c, 6, ctypes.byref(st))
-        d = lib.ndt_tensor_f64_data(p)  # device -> host read of the result
-        ok = bool(d) and st.value == 0
-        lib.ndt_tensor_f64_release(p)
-        lib.ndt_tensor_f64_release(t)
-        return ok
-
-    for _ in range(3):
-        e2e_step()
-    e2e_steps = max(5, min(args.steps, 40))
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
-    w0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        assert e2e_step()
-    torch.cuda.synchronize()
-    w = torch.tensor([time.perf_counter() - w0], device="cuda")
-    if pg:
-        pg.all_reduce(w, op=pg.ReduceOp.MAX)
-    e2e = {"value": BYTES_F64 * e2e_steps * world / float(w.item()) / 1e9, "unit": "GB/s",
+        assert lib.ndt_tensor_f64_data(p) and st.value == 0
+        held += [t, p]
+    for h in held:
+        lib.ndt_tensor_f64_release(h)
+    e2e_run(4 * E2E_THREADS, E2E_THREADS)
+    e2e_steps = max(6, min(args.steps, 40))
+    t_multi = e2e_run(e2e_steps, E2E_THREADS)
+    t_single = e2e_run(e2e_steps, 1)
+    e2e = {"value": BYTES_F64 * e2e_steps * world / t_multi / 1e9, "unit": "GB/s",
            "h2d_bytes_per_step": NELEM * 8, "d2h_bytes_per_step": NELEM * 8,
-           "path": "ndt_tensor_f64_from_data (pinned host) -> ndt_tensor_f64_permutedims -> ndt_tensor_f64_data"}
+           "host_threads": E2E_THREADS,
+           "single_thread_value": BYTES_F64 * e2e_steps * world / t_single / 1e9,
+           "path": "ndt_tensor_f64_from_data (pinned host) -> ndt_tensor_f64_permutedims -> ndt_tensor_f64_data, "
+                   f"steps split over {E2E_THREADS} host threads"}
 
     # ---- extras: complex permute and the dense f64 MPS merge (DMMA GEMM)
     extras = [batched_line]

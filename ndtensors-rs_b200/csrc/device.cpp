@@ -1,4 +1,5 @@
 // Per-device context: streams, stream-ordered device pool, pinned host cache.
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -58,6 +59,7 @@ DeviceCtx& ctx(int device) {
   NDT_CUDA(cudaStreamCreateWithFlags(&c->compute, cudaStreamNonBlocking));
   c->own_compute = c->compute;
   NDT_CUDA(cudaStreamCreateWithFlags(&c->upload, cudaStreamNonBlocking));
+  NDT_CUDA(cudaStreamCreateWithFlags(&c->download, cudaStreamNonBlocking));
   NDT_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
   int optin = 0;
   NDT_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
@@ -167,8 +169,8 @@ void empty_caches() {
   }
 }
 
-static uint64_t g_launches = 0;
-uint64_t launch_count() { return g_launches; }
-void count_launch() { ++g_launches; }
+static std::atomic<uint64_t> g_launches{0};
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 }  // namespace ndt

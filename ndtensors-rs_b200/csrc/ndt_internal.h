@@ -78,6 +78,7 @@ struct DeviceCtx {
   cudaStream_t compute = nullptr;  // all kernels of the library
   cudaStream_t own_compute = nullptr;  // the library's own compute stream
   cudaStream_t upload = nullptr;   // host->device copies of caller data
+  cudaStream_t download = nullptr; // device->host reads of results
   bool external_stream = false;    // compute stream supplied by the caller
   int sm_count = 0;
   size_t smem_optin = 0;

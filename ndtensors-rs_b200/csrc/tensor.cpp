@@ -61,9 +61,20 @@ void* Storage::host_read() {
   if (uniform) {
     host_fill(dt, host, len, fill_re, fill_im);
   } else if (dev_valid) {
+    // Read on the download stream once the compute stream's work so far is
+    // done, and wait for this copy only: the compute stream stays free, so
+    // another host thread's upload and kernels overlap this read.
     DeviceCtx& c = ctx(device);
-    NDT_CUDA(cudaMemcpyAsync(host, dev, bytes(), cudaMemcpyDeviceToHost, c.compute));
-    NDT_CUDA(cudaStreamSynchronize(c.compute));
+    cudaEvent_t ready, done;
+    NDT_CUDA(cudaEventCreateWithFlags(&ready, cudaEventDisableTiming));
+    NDT_CUDA(cudaEventCreateWithFlags(&done, cudaEventDisableTiming));
+    NDT_CUDA(cudaEventRecord(ready, c.compute));
+    NDT_CUDA(cudaStreamWaitEvent(c.download, ready, 0));
+    NDT_CUDA(cudaMemcpyAsync(host, dev, bytes(), cudaMemcpyDeviceToHost, c.download));
+    NDT_CUDA(cudaEventRecord(done, c.download));
+    NDT_CUDA(cudaEventSynchronize(done));
+    cudaEventDestroy(ready);
+    cudaEventDestroy(done);
   } else {
     memset(host, 0, bytes());
   }
@@ -164,9 +175,12 @@ Dense make_from_host(DType dt, const void* data, size_t len, const std::vector<s
   t.st = std::make_shared<Storage>(dt, len);
   Storage& s = *t.st;
   if (device_available()) {
-    // Upload straight from the caller's buffer on the upload stream; the
-    // compute stream waits for it.  The call returns once the caller's
-    // buffer has been consumed, so the caller may reuse it immediately.
+    // Upload straight from the caller's buffer on the upload stream.  The
+    // call returns once the copy has completed, so the caller may reuse its
+    // buffer at once, and every kernel enqueued afterwards sees the data
+    // without a stream dependency: the compute stream never waits on an
+    // upload, and one host thread's kernels and read-back do not queue
+    // behind another thread's upload.
     int d = current_device();
     DeviceCtx& c = ctx(d);
     s.device = d;
@@ -177,7 +191,6 @@ Dense make_from_host(DType dt, const void* data, size_t len, const std::vector<s
     NDT_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     NDT_CUDA(cudaMemcpyAsync(p, data, s.bytes(), cudaMemcpyHostToDevice, c.upload));
     NDT_CUDA(cudaEventRecord(ev, c.upload));
-    NDT_CUDA(cudaStreamWaitEvent(c.compute, ev, 0));
     NDT_CUDA(cudaEventSynchronize(ev));
     cudaEventDestroy(ev);
     s.dev_valid = true;

@@ -136,3 +136,46 @@ def test_permute_raw_device_entry(gpu, oracle):
     bad = lib.ndt_b200_permutedims_dev(0, ctypes.c_void_p(src.data_ptr()), ctypes.c_void_p(dst.data_ptr()),
                                        (SZ * 4)(*shape), 4, (SZ * 4)(0, 0, 1, 2), 4, None)
     assert bad == -5
+
+
+def test_abi_concurrent_host_threads(gpu, oracle):
+    """Several host threads drive the C ABI at once (from_data -> permutedims
+    -> data on their own handles): uploads, kernels and read-backs of
+    different threads interleave on the library's streams, every result
+    stays bit-exact."""
+    import threading
+
+    import torch
+
+    lib = gpu.get_lib()
+    dev = torch.cuda.current_device()
+    shape, perm = (24, 7, 5, 33), (3, 1, 0, 2)
+    rng = np.random.default_rng(77)
+    inputs = [np.asfortranarray(rng.standard_normal(shape)) for _ in range(6)]
+    refs = [oracle.permutedims(x, perm)[1] for x in inputs]
+    shape_c, perm_c = (SZ * 4)(*shape), (SZ * 4)(*perm)
+    bad = []
+
+    def worker(idx):
+        torch.cuda.set_device(dev)
+        st = ctypes.c_int(-999)
+        for rep in range(5):
+            for i in idx:
+                x = inputs[i]
+                t = lib.ndt_tensor_f64_from_data(x.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), x.size, shape_c,
+                                                 4, ctypes.byref(st))
+                p = lib.ndt_tensor_f64_permutedims(t, perm_c, 4, ctypes.byref(st))
+                d = lib.ndt_tensor_f64_data(p)
+                got = np.ctypeslib.as_array(d, shape=(x.size,)).copy() if d else None
+                if st.value != 0 or got is None or not np.array_equal(_bits(got), _bits(refs[i])):
+                    bad.append((i, rep, st.value))
+                lib.ndt_tensor_f64_release(p)
+                lib.ndt_tensor_f64_release(t)
+
+    ths = [threading.Thread(target=worker, args=([0, 2, 4],)), threading.Thread(target=worker, args=([1, 3, 5],)),
+           threading.Thread(target=worker, args=([5, 0, 3],))]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    assert not bad, bad[:5]
