@@ -348,6 +348,25 @@ def cpu_contraction_baselines():
     return out
 
 
+def host_info():
+    """CPU model, logical cores and RAM of the host the CPU legs ran on."""
+    cpu, ram = None, None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    cpu = ln.split(":", 1)[1].strip()
+                    break
+        with open("/proc/meminfo") as f:
+            for ln in f:
+                if ln.startswith("MemTotal"):
+                    ram = round(int(ln.split()[1]) / 1024 ** 2, 1)
+                    break
+    except OSError:
+        pass
+    return {"cpu": cpu, "logical_cores": os.cpu_count(), "ram_gib": ram}
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return  # rank 0 alone runs the host-CPU reference
@@ -376,6 +395,7 @@ def run_reference(args, world, rank):
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
                          "sample": f"full 16^6 f64 tensor per step, {threads} host threads over the source index range"},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "host": host_info(),
     }
     print(json.dumps(line), flush=True)
 
@@ -648,6 +668,7 @@ def main():
             "e2e": e2e,
             "gpu_launches": int(launches),
             "clocks": sampler.result(),
+            "host": host_info(),
             "contraction": extras,
         }
         print(json.dumps(line), flush=True)
@@ -718,10 +739,8 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     flops5 = W.flops_blocksparse((sa, ca, None), [1, 2, -1], (sb, cb, None), [-1, 3, 4], True)
 
     def chain():
-        AS = bs.contract_diag(A, [1, 2, -1], S, [-1, 3])
-        if world == 1:
-            return bs.contract(AS, [1, 2, -1], B, [-1, 3, 4])
-        return bs.contract_shard(AS, [1, 2, -1], B, [-1, 3, 4], rank, world)
+        # one grouped launch per rank: S's diagonal scales A's loads (no A.S pass)
+        return bs.contract_through_diag(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], rank, world)
 
     ms5, _ = timed(chain, 10)
     tf5 = flops5 / (ms5 * 1e-3) / 1e12

@@ -200,8 +200,9 @@ const double* ndt_blocksparse_f64_device_ptr(const ndt_blocksparse_f64* t); /* d
 ndt_blocksparse_f64* ndt_blocksparse_f64_contract(const ndt_blocksparse_f64* a, const long* labels_a,
                                                   size_t ndim_a, const ndt_blocksparse_f64* b, const long* labels_b,
                                                   size_t ndim_b, int* status);
-/* The output blocks of `rank`'s FLOP-balanced contiguous range of the sorted output block list
- * (contract_blocksparse split over nranks processes / GPUs; no collective). */
+/* `rank`'s FLOP-balanced share of the output blocks (contract_blocksparse split over nranks
+ * processes / GPUs; no collective): blocks go to ranks heaviest first, each to the least loaded
+ * rank (ties to the lower rank); the returned blocks are sorted. */
 ndt_blocksparse_f64* ndt_blocksparse_f64_contract_shard(const ndt_blocksparse_f64* a, const long* labels_a,
                                                         size_t ndim_a, const ndt_blocksparse_f64* b,
                                                         const long* labels_b, size_t ndim_b, int rank, int nranks,
@@ -297,6 +298,20 @@ ndt_blocksparse_c64* ndt_diagblocksparse_c64_to_blocksparse(const ndt_diagblocks
 ndt_blocksparse_c64* ndt_blocksparse_c64_contract_diag(const ndt_blocksparse_c64* a, const long* labels_a,
                                                        size_t ndim_a, const ndt_diagblocksparse_c64* s,
                                                        const long* labels_s, size_t ndim_s, int* status);
+/* (A . S) . B with S a rank-2 diagonal between A and B (no counterpart in the reference): labels_s
+ * = {x, y}, both negative; x labels one axis of A, y one axis of B, and every other label of A and B
+ * is positive.  Equals contract(contract_diag(A, S), B): A's and B's free axes in label order.  One
+ * grouped launch that scales A's contracted index by S's diagonal as it loads A (no A . S
+ * intermediate) when S's blocks are square and each coordinate of A's contracted axis meets one S
+ * block; otherwise the two contractions in turn.  rank / nranks as in contract_shard (0, 1: all). */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_through_diag(
+    const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a, const ndt_diagblocksparse_f64* s,
+    const long* labels_s, size_t ndim_s, const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b, int rank,
+    int nranks, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_through_diag(
+    const ndt_blocksparse_c64* a, const long* labels_a, size_t ndim_a, const ndt_diagblocksparse_c64* s,
+    const long* labels_s, size_t ndim_s, const ndt_blocksparse_c64* b, const long* labels_b, size_t ndim_b, int rank,
+    int nranks, int* status);
 
 /* Dense f64 contraction that allocates no memory (no counterpart in the
  * reference).  For callers that may not call cudaMalloc -- allocation-free

@@ -17,6 +17,7 @@
 // Operand blocks whose axes are not already [free..., contracted...] (A) /
 // [contracted..., free...] (B) are permuted block by block first (TTGT).
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <map>
 #include <set>
@@ -70,6 +71,7 @@ struct BlockSparseT {
 
 struct DiagBlockSparseT {
   BlockSparseT s;  // coords / block sizes; offs are diagonal offsets
+  bool real_valued = true;  // complex values with all imaginary parts zero (set on upload)
   size_t diag_size(const std::vector<size_t>& c) const {
     if (c.empty()) return 0;
     size_t m = SIZE_MAX;
@@ -138,11 +140,26 @@ bool is_prefix_run(const std::vector<size_t>& v, size_t start) {
 }  // namespace
 
 // contract_blocksparse (contract/blocksparse.rs:87-183).  With nranks > 1 only
-// the output blocks of this rank's FLOP-balanced contiguous range of the
-// sorted output block list are computed (and stored).
+// this rank's output blocks are computed (and stored): output blocks go to
+// ranks by longest processing time first on their tensor-core tile cost
+// (costliest block to the least loaded rank, ties to the lower rank), so the
+// per-rank costs differ by at most one block's.  Every rank derives the same
+// assignment from the same operands.
 struct ShardPlan {
   std::vector<size_t> blocks;  // output blocks per rank
   std::vector<double> flops;   // real flop per rank
+};
+
+// A rank-2 diagonal operand S between A and B, contracted with A's axis
+// `a_axis` on one side and with B on the other: S block (q_a, q_b) maps A's
+// coordinate q_a on that axis to B's coordinate q_b, and its diagonal starts
+// at `off` in S's packed values.  The grouped GEMM scales A's k index by
+// those values as it loads A, so A . S is never formed.
+struct ThroughDiag {
+  size_t a_axis = 0;
+  std::map<size_t, std::pair<size_t, int64_t>> qmap;  // q_a -> (q_b, off)
+  const void* sdata = nullptr;
+  bool real = false;  // every diagonal value real (one multiply per component)
 };
 
 // `select` (nsel output coordinates of rank |ua| + |ub|, natural order):
@@ -150,7 +167,7 @@ struct ShardPlan {
 // rank's share when its operands hold only the blocks that share references.
 BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
                          const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
-                         const size_t* select = nullptr, size_t nsel = 0) {
+                         const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr) {
   const size_t na = A.ndim(), nb = B.ndim();
   if (A.dt != B.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
   if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
@@ -171,7 +188,12 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   for (size_t j = 0; j < nb; j++)
     if (std::find(pb.begin(), pb.end(), j) == pb.end()) ub.push_back(j);
   // blocksparse.rs:114-132: same block count and sizes on contracted axes
+  size_t td_pos = SIZE_MAX;  // position of the diagonal's axis among the contracted pairs
   for (size_t p = 0; p < pa.size(); p++) {
+    if (td && pa[p] == td->a_axis) {
+      td_pos = p;  // sizes checked against the diagonal operand by the caller
+      continue;
+    }
     if (A.bsz[pa[p]].size() != B.bsz[pb[p]].size()) throw Error(ErrKind::ShapeMismatch, "block counts differ");
     for (size_t q = 0; q < A.bsz[pa[p]].size(); q++)
       if (A.bsz[pa[p]][q] != B.bsz[pb[p]][q]) throw Error(ErrKind::ShapeMismatch, "block sizes differ");
@@ -193,7 +215,13 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   for (size_t b = 0; b < B.nnzb(); b++) bmap[key_of(B.coords[b], pb)].push_back(b);
   std::map<std::vector<size_t>, std::vector<std::pair<size_t, size_t>>> contrib;  // sorted output blocks
   for (size_t a = 0; a < A.nnzb(); a++) {
-    auto it = bmap.find(key_of(A.coords[a], pa));
+    std::vector<size_t> key = key_of(A.coords[a], pa);
+    if (td_pos != SIZE_MAX) {  // through the diagonal: A's q_a meets B's q_b
+      auto q = td->qmap.find(key[td_pos]);
+      if (q == td->qmap.end()) continue;
+      key[td_pos] = q->second.first;
+    }
+    auto it = bmap.find(key);
     if (it == bmap.end()) continue;
     for (size_t b : it->second) {
       std::vector<size_t> oc;
@@ -241,47 +269,53 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   for (size_t i = 0; i < perm_c.size(); i++)
     if (olab[perm_c[i]] != olab[i]) permute_c = true;
 
-  // sorted output blocks; FLOP-balanced contiguous range for this rank
+  // sorted output blocks with their real flops and their cost on the
+  // tensor cores: tiles of 64 x 64, k in steps of 16 (a block much smaller
+  // than a tile costs a whole tile)
   std::vector<std::vector<size_t>> all_out;
-  std::vector<double> work;
+  std::vector<double> work, cost;
   const double cf = A.dt == DType::C128 ? 8.0 : 2.0;
   for (auto& kv : contrib) {
     all_out.push_back(kv.first);
-    double w = 0;
+    double w = 0, c = 0;
     for (auto& pr : kv.second) {
       double m = 1, n = 1, k = 1;
       for (size_t i : ua) m *= (double)A.bsz[i][A.coords[pr.first][i]];
       for (size_t j : ub) n *= (double)B.bsz[j][B.coords[pr.second][j]];
       for (size_t i : pa) k *= (double)A.bsz[i][A.coords[pr.first][i]];
       w += cf * m * n * k;
+      c += std::ceil(m / 64) * std::ceil(n / 64) * std::ceil(k / 16);
     }
     work.push_back(w);
+    cost.push_back(c);
   }
-  // Contiguous ranges of the sorted output blocks, cut where the running
-  // FLOP sum crosses r/nranks of the total (an output block is never split).
-  std::vector<size_t> cut(nranks + 1, all_out.size());
-  cut[0] = 0;
+  // Longest processing time first on the tile cost: costliest output block
+  // to the least loaded rank (stable order, ties to the lower rank).
+  std::vector<int> owner(all_out.size(), 0);
   {
-    double tot = 0;
-    for (double w : work) tot += w;
-    double acc = 0;
-    int r = 1;
-    for (size_t i = 0; i < all_out.size() && r < nranks; i++) {
-      acc += work[i];
-      while (r < nranks && acc >= tot * r / nranks) cut[r++] = i + 1;
+    std::vector<double> load(nranks, 0.0);
+    std::vector<size_t> order(all_out.size());
+    for (size_t i = 0; i < order.size(); i++) order[i] = i;
+    std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return cost[x] > cost[y]; });
+    for (size_t i : order) {
+      int r = 0;
+      for (int q = 1; q < nranks; q++)
+        if (load[q] < load[r]) r = q;
+      owner[i] = r;
+      load[r] += cost[i];
     }
   }
   if (plan_only) {
     plan_only->blocks.assign(nranks, 0);
     plan_only->flops.assign(nranks, 0.0);
-    for (int r = 0; r < nranks; r++) {
-      plan_only->blocks[r] = cut[r + 1] - cut[r];
-      for (size_t i = cut[r]; i < cut[r + 1]; i++) plan_only->flops[r] += work[i];
+    for (size_t i = 0; i < owner.size(); i++) {
+      plan_only->blocks[owner[i]]++;
+      plan_only->flops[owner[i]] += work[i];
     }
     return C;
   }
-  const size_t lo = cut[rank], hi = cut[rank + 1];
-  for (size_t i = lo; i < hi; i++) C.coords.push_back(all_out[i]);
+  for (size_t i = 0; i < all_out.size(); i++)
+    if (owner[i] == rank) C.coords.push_back(all_out[i]);
   C.pack();
   C.st = std::make_shared<Storage>(C.dt, C.total());
   if (C.total() == 0 || contrib.empty()) {
@@ -364,14 +398,15 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
       sg.k = k;
       sg.lda = a_kmajor ? k : m;
       sg.ldb = b_kmajor ? k : n;
-      sg.scale_off = -1;
+      sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
       segs.push_back(sg);
     }
     probs.push_back(pr);
   }
   void* Cd = C.st->dev_overwrite();
   void* Cu = permute_c ? dev_alloc(C.total() * es, dev) : Cd;
-  grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, nullptr, s);
+  grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, td_pos != SIZE_MAX ? td->sdata : nullptr, s,
+               td_pos != SIZE_MAX && td->real);
   if (permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,
     // checked above); the data is permuted block by block.
@@ -630,6 +665,76 @@ BlockSparseT bs_contract_diag(const BlockSparseT& A, const std::vector<int32_t>&
   void* cd = C.st->dev_overwrite();
   bs_diag_scale(A.dt, A.st->dev_read(), t.st->dev_read(), cd, offs, tab, (int64_t)C.total(), ctx().compute);
   return C;
+}
+
+// (A . S) . B with S a rank-2 diagonal operand whose two labels are the only
+// contracted ones: S's first label is contracted with A (one axis), its second
+// with B (one axis); every other label of A and B is positive.  The result is
+// contract(contract_diag(A, la, S, (x, P)), sorted(A's labels) ++ (y), B, lb)
+// for a fresh positive P, i.e. the A-free ++ B-free axes in label order.
+// When S's blocks are square and each of A's coordinates on the contracted
+// axis meets at most one S block, this is ONE grouped launch whose A loads are
+// scaled by S's diagonal (no A . S intermediate); otherwise the two
+// contractions run one after the other.  rank / nranks: this rank's share of
+// the output blocks, as contract_shard assigns them.
+BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<int32_t>& la,
+                                      const DiagBlockSparseT& S, const std::vector<int32_t>& ls,
+                                      const BlockSparseT& B, const std::vector<int32_t>& lb, int rank, int nranks) {
+  const BlockSparseT& t = S.s;
+  if (la.size() != A.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
+  if (lb.size() != B.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_b length != ndim(b)");
+  if (ls.size() != 2 || t.ndim() != 2)
+    throw Error(ErrKind::InvalidArgument, "the diagonal operand must be rank 2 with two labels");
+  const int32_t x = ls[0], y = ls[1];
+  if (x >= 0 || y >= 0 || x == y)
+    throw Error(ErrKind::InvalidArgument, "both labels of the diagonal operand must be negative and distinct");
+  size_t ax_a = SIZE_MAX, ax_b = SIZE_MAX;
+  int32_t pmax = 0;
+  for (size_t i = 0; i < la.size(); i++) {
+    if (la[i] == x && ax_a == SIZE_MAX)
+      ax_a = i;
+    else if (la[i] <= 0)
+      throw Error(ErrKind::InvalidArgument, "A's labels other than the diagonal's must be positive and single");
+    pmax = std::max(pmax, la[i]);
+  }
+  for (size_t j = 0; j < lb.size(); j++) {
+    if (lb[j] == y && ax_b == SIZE_MAX)
+      ax_b = j;
+    else if (lb[j] <= 0)
+      throw Error(ErrKind::InvalidArgument, "B's labels other than the diagonal's must be positive and single");
+    pmax = std::max(pmax, lb[j]);
+  }
+  if (ax_a == SIZE_MAX || ax_b == SIZE_MAX)
+    throw Error(ErrKind::InvalidArgument, "A must carry the diagonal's first label and B its second");
+  for (int32_t u : la)
+    for (int32_t v : lb)
+      if (u == v) throw Error(ErrKind::InvalidArgument, "A and B may share no label");
+  bool fused = A.dt == B.dt && A.dt == t.dt && A.bsz[ax_a] == t.bsz[0] && t.bsz[1] == B.bsz[ax_b];
+  ThroughDiag td;
+  td.a_axis = ax_a;
+  for (size_t b = 0; b < t.nnzb() && fused; b++) {
+    const size_t qa = t.coords[b][0], qb = t.coords[b][1];
+    if (t.bsz[0][qa] != t.bsz[1][qb] || td.qmap.count(qa)) fused = false;
+    td.qmap[qa] = {qb, (int64_t)t.offs[b]};
+  }
+  if (fused) {
+    td.sdata = t.nnzb() ? t.st->dev_read() : nullptr;
+    td.real = S.real_valued;
+    if (!td.sdata) fused = false;
+  }
+  if (fused) {
+    std::vector<int32_t> lb2(lb);
+    lb2[ax_b] = x;  // pair A's axis with B's through the diagonal
+    return bs_contract(A, la, B, lb2, rank, nranks, nullptr, nullptr, 0, &td);
+  }
+  const int32_t P = pmax + 1;
+  BlockSparseT AS = bs_contract_diag(A, la, S, {x, P});
+  std::vector<int32_t> las;
+  for (int32_t u : la)
+    if (u != x) las.push_back(u);
+  std::sort(las.begin(), las.end());
+  las.push_back(y);
+  return bs_contract(AS, las, B, lb, rank, nranks);
 }
 
 }  // namespace ndt
@@ -973,6 +1078,8 @@ NDT_BS_FROM_DENSE(ndt_blocksparse_c64, ndt_tensor_c64, c64)
       DiagBlockSparseT S = make_diag(DTYPE_##DT, bsz, cs);                                                              \
       if (len != S.s.total()) throw Error(ErrKind::ShapeMismatch, "diag length != total diagonal elements");            \
       if (len) S.s.st = make_from_host(DTYPE_##DT, diag, len, {len}).st;                                                \
+      if (DTYPE_##DT == DType::C128)                                                                                    \
+        for (size_t i = 0; i < len && S.real_valued; i++) S.real_valued = diag[2 * i + 1] == 0.0;                       \
       return new NdtDiag{S};                                                                                            \
     });                                                                                                                 \
   }                                                                                                                     \
@@ -1003,6 +1110,19 @@ NDT_BS_FROM_DENSE(ndt_blocksparse_c64, ndt_tensor_c64, c64)
     }                                                                                                                   \
     return (TB*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                    \
       return new NdtBs{bs_contract_diag(((const NdtBs*)a)->t, labels(la, na), ((const NdtDiag*)s)->t, labels(ls, ns))}; \
+    });                                                                                                                 \
+  }                                                                                                                     \
+  TB* ndt_blocksparse_##DT##_contract_through_diag(const TB* a, const long* la, size_t na, const T* s, const long* ls,  \
+                                                   size_t ns, const TB* b, const long* lb, size_t nb, int rank,         \
+                                                   int nranks, int* status) {                                          \
+    if (!status) return nullptr;                                                                                        \
+    if (!a || !s || !b || (!la && na) || (!ls && ns) || (!lb && nb) || nranks < 1 || rank < 0 || rank >= nranks) {     \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                    \
+      return new NdtBs{bs_contract_through_diag(((const NdtBs*)a)->t, labels(la, na), ((const NdtDiag*)s)->t,           \
+                                                labels(ls, ns), ((const NdtBs*)b)->t, labels(lb, nb), rank, nranks)};   \
     });                                                                                                                 \
   }
 NDT_DIAG(ndt_diagblocksparse_f64, ndt_tensor_f64, ndt_blocksparse_f64, f64)

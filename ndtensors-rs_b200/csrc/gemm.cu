@@ -25,6 +25,8 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <queue>
+#include <vector>
 
 #include "ndt_internal.h"
 
@@ -42,6 +44,8 @@ struct KArgs {
   const int4* tiles;  // x = problem, y = tile m index, z = tile n index
   const GroupedProblem* probs;
   const GroupedSegment* segs;
+  const void* kscale;  // grouped mode: per-k scale of A (segments' scale_off), or null
+  int kscale_real;     // complex scale values whose imaginary parts are all zero
   int accumulate;
 };
 
@@ -83,7 +87,8 @@ struct Pitch {
   static constexpr int elems = rows * value;
 };
 
-template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM>
+template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM,
+          int SCALE = 0>
 struct Cfg {
   static constexpr int kThreads = WM_WARPS * WN_WARPS * 32;
   static constexpr int WM = BM / WM_WARPS;  // warp tile rows
@@ -93,7 +98,8 @@ struct Cfg {
   static constexpr int ES = CPLX ? 16 : 8;
   using PA = Pitch<CPLX, AK, BM, BK>;
   using PB = Pitch<CPLX, BKM, BN, BK>;
-  static constexpr int stage_elems = PA::elems + PB::elems;
+  // SCALE: each stage also holds the BK scale values of its k range
+  static constexpr int stage_elems = PA::elems + PB::elems + (SCALE ? BK : 0);
   static constexpr size_t smem_bytes = (size_t)STAGES * stage_elems * ES;
 };
 
@@ -109,12 +115,18 @@ struct CopyPlan {
 
 // VEC (f64 only): 16-byte pair copies along the contiguous index; a pair
 // crossing the matrix edge copies 8 bytes and zero-fills the rest.
+// SCALE (grouped only): A(i, k) is multiplied by kscale[scale_off + k] of its
+// segment as its fragments leave shared memory, so a diagonal operand between
+// A and B (A . diag(s) . B) costs no pass of its own over A.  1: real scale
+// values (f64, or complex ones with zero imaginary parts: one multiply per
+// real component), 2: complex scale values (a complex multiply).
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
-          bool GROUPED>
+          bool GROUPED, int SCALE>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(const __grid_constant__ KArgs args) {
   pdl_release();
   pdl_wait();  // before the first global access (tile tables, operands)
-  using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM>;
+  static_assert(SCALE == 0 || GROUPED, "k-scaling is a grouped-mode feature");
+  using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM, SCALE>;
   constexpr int NTH = C::kThreads, MT = C::MT, NT = C::NT, ES = C::ES;
   constexpr int LDA = C::PA::value, LDB = C::PB::value;
   constexpr int RPL = CPLX ? 2 : 1;  // doubles per element
@@ -173,7 +185,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
 
   // ---- load iterator over (segment, k0)
   int64_t seg = seg_begin, seg_end = seg_begin + seg_count;
-  int64_t a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0;
+  int64_t a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0, s_off = 0;
   auto load_seg = [&](int64_t s) {
     if constexpr (!GROUPED) {
       kseg = args.k;
@@ -186,6 +198,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
       kseg = sd.k;
       lda = sd.lda;
       ldb = sd.ldb;
+      s_off = sd.scale_off;
     }
   };
   int total_steps = 0;
@@ -242,6 +255,18 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
           cp_async16n(d, p, nb * 16);
         else
           cp_async8(d, p, nb != 0);
+      }
+    }
+    // ---- the stage's BK scale values (zero past the segment's end)
+    if constexpr (SCALE != 0) {
+      double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
+      if (tid < BK) {
+        const bool ok = tid < krem;
+        const char* src = (const char*)args.kscale + (s_off + (ok ? k0 + tid : 0)) * ES;
+        if constexpr (CPLX)
+          cp_async16n(Ss + tid * 2, src, ok ? 16 : 0);
+        else
+          cp_async8(Ss + tid, src, ok);
       }
     }
   };
@@ -310,6 +335,40 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
             ai[i][q] = v.y;
           } else {
             a[i][q] = As[idx];
+          }
+        }
+      }
+      if constexpr (SCALE != 0) {
+        // A(i, k) * s(k): fragment column t + 4 (q >> 1) of this k8 step
+        const double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          const int col = kk + t + 4 * h;
+          if constexpr (CPLX && SCALE == 2) {
+            const double2 sv = *reinterpret_cast<const double2*>(Ss + (size_t)col * 2);
+#pragma unroll
+            for (int i = 0; i < MT; i++)
+#pragma unroll
+              for (int q = 2 * h; q < 2 * h + 2; q++) {
+                const double re = a[i][q], im = ai[i][q];
+                a[i][q] = re * sv.x - im * sv.y;
+                ai[i][q] = re * sv.y + im * sv.x;
+              }
+          } else if constexpr (CPLX) {
+            const double sv = Ss[(size_t)col * 2];
+#pragma unroll
+            for (int i = 0; i < MT; i++)
+#pragma unroll
+              for (int q = 2 * h; q < 2 * h + 2; q++) {
+                a[i][q] *= sv;
+                ai[i][q] *= sv;
+              }
+          } else {
+            const double sv = Ss[col];
+#pragma unroll
+            for (int i = 0; i < MT; i++)
+#pragma unroll
+              for (int q = 2 * h; q < 2 * h + 2; q++) a[i][q] *= sv;
           }
         }
       }
@@ -386,10 +445,11 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
       }
 }
 
-template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED>
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED,
+          int SCALE>
 void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
-  using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM>;
-  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED>;
+  using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, SCALE>;
+  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED, SCALE>;
   ensure_dynamic_smem((const void*)kern, C::smem_bytes);
   launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
   count_launch();
@@ -399,9 +459,13 @@ void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
 template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC>
 void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
   if (a.tiles == nullptr)
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, false>(a, grid, s);
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, false, 0>(a, grid, s);
+  else if (a.kscale == nullptr)
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, 0>(a, grid, s);
+  else if (!CPLX || a.kscale_real)
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, 1>(a, grid, s);
   else
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true>(a, grid, s);
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, CPLX ? 2 : 1>(a, grid, s);
 }
 
 // Tile classes, indexed by `cls`, with their steady-state rate relative to
@@ -544,42 +608,59 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
 
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* /*kscale*/, cudaStream_t s) {
+                  const void* kscale, cudaStream_t s, bool kscale_real) {
   if (probs.empty()) return;
   const bool cplx = dt == DType::C128;
   const DeviceCtx& c = ctx();
-  // Tile list: every (problem, tile) with its work (tile area x total k),
-  // heaviest first so the tail of the launch is made of small tiles.
-  auto build = [&](int cl, std::vector<int4>& tiles, double* eff) {
+  // Tile list: every (problem, tile) with its k length, heaviest first so
+  // the tail of the launch is made of short tiles.  Each class is scored by
+  // its estimated time: the makespan of placing the tiles in that order on
+  // the SM slots, each on the slot that frees first (the way the block
+  // scheduler hands them out), times the class's cost per k-step.  Grids of
+  // more than 64 waves use the mean load (their tail is negligible).
+  auto build = [&](int cl, std::vector<int4>& tiles, double* time) {
     const TileClass& tc = tile_class(cplx, cl);
     const int bm = tc.bm, bn = tc.bn;
-    std::vector<std::pair<double, int4>> w;
-    double useful = 0, padded = 0;
+    const int bk = cplx ? 16 : 32;
+    std::vector<std::pair<int64_t, int4>> w;
     for (size_t p = 0; p < probs.size(); p++) {
       const GroupedProblem& pr = probs[p];
       int64_t ktot = 0;
-      for (int64_t q = pr.seg_begin; q < pr.seg_begin + pr.seg_count; q++) ktot += segs[q].k;
+      for (int64_t q = pr.seg_begin; q < pr.seg_begin + pr.seg_count; q++) ktot += (segs[q].k + bk - 1) / bk;
       int64_t mt = (pr.m + bm - 1) / bm, nt = (pr.n + bn - 1) / bn;
-      useful += (double)pr.m * pr.n * ktot;
-      padded += (double)mt * bm * nt * bn * ((ktot + 15) / 16 * 16);
       for (int64_t i = 0; i < mt; i++)
-        for (int64_t j = 0; j < nt; j++) w.push_back({(double)ktot, make_int4((int)p, (int)i, (int)j, 0)});
+        for (int64_t j = 0; j < nt; j++) w.push_back({ktot, make_int4((int)p, (int)i, (int)j, 0)});
     }
     std::stable_sort(w.begin(), w.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
     tiles.resize(w.size());
     for (size_t i = 0; i < w.size(); i++) tiles[i] = w[i].second;
-    double slots = (double)c.sm_count * tc.per_sm;
-    double waves = std::ceil((double)tiles.size() / slots);
-    *eff = useful / padded * std::min(1.0, (double)tiles.size() / (waves * slots)) * tc.rate;
+    const int64_t slots = (int64_t)c.sm_count * tc.per_sm;
+    double span = 0;
+    if ((int64_t)w.size() <= 64 * slots) {
+      std::priority_queue<int64_t, std::vector<int64_t>, std::greater<int64_t>> free_at;
+      for (int64_t i = 0; i < slots; i++) free_at.push(0);
+      for (const auto& x : w) {
+        int64_t t0 = free_at.top();
+        free_at.pop();
+        free_at.push(t0 + x.first);
+        span = std::max(span, (double)(t0 + x.first));
+      }
+    } else {
+      for (const auto& x : w) span += (double)x.first;
+      span /= (double)slots;
+    }
+    // one k-step of a bm x bn tile on a slot that shares its SM with
+    // per_sm - 1 others, at the class's relative rate
+    *time = span * ((double)bm * bn * bk * tc.per_sm / tc.rate);
   };
   std::vector<int4> tiles, cand;
   int cls = 0;
   double best = -1;
   for (int cl = 0; cl < nclasses(cplx); cl++) {
-    double e;
-    build(cl, cand, &e);
-    if (e > best) {
-      best = e;
+    double t;
+    build(cl, cand, &t);
+    if (best < 0 || t < best) {
+      best = t;
       cls = cl;
       tiles.swap(cand);
     }
@@ -603,6 +684,8 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.tiles = (const int4*)(d + off_t);
   a.probs = (const GroupedProblem*)d;
   a.segs = (const GroupedSegment*)(d + off_s);
+  a.kscale = kscale;
+  a.kscale_real = kscale_real ? 1 : 0;
   a.accumulate = 0;
   int grid = (int)tiles.size();
   bool vec = aligned16(A) && aligned16(B);

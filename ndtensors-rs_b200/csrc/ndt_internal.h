@@ -241,7 +241,7 @@ struct GroupedSegment {
 };
 void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* kscale, cudaStream_t s);
+                  const void* kscale, cudaStream_t s, bool kscale_real = false);
 
 // Block-sparse device helpers (blocksparse_kernels.cu).  A block table entry
 // describes one block: its extents, and for the dense side its start offset

@@ -133,6 +133,9 @@ SIGNATURES = [
             (f"ndt_diagblocksparse_{dt}_to_blocksparse", vp, [vp, c_int_p]),
             (f"ndt_blocksparse_{dt}_contract_diag", vp,
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_through_diag", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t,
+              ctypes.c_int, ctypes.c_int, c_int_p]),
         ]
     ],
     (

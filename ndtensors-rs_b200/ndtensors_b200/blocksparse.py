@@ -284,7 +284,9 @@ def contract(a, labels_a, b, labels_b):
 
 
 def contract_shard(a, labels_a, b, labels_b, rank: int, nranks: int):
-    """This rank's FLOP-balanced share of the output blocks (no collective)."""
+    """This rank's FLOP-balanced share of the output blocks (no collective):
+    output blocks go to ranks heaviest first, each to the least loaded rank,
+    so every rank derives the same assignment from the same operands."""
     la, na = _labels(labels_a)
     lb, nb = _labels(labels_b)
     st = ctypes.c_int(-999)
@@ -330,13 +332,14 @@ def allgather(shard, group=None):
     into the full block-sparse tensor on all ranks, with torch.distributed.
     Blocks come out sorted, as contract_blocksparse orders them.
 
-    Shards are contiguous ranges of the sorted output block list, so rank r's
-    packed data is the r-th contiguous range of the gathered data.  Two
-    collectives: the per-rank lengths, then one all_gather of every rank's
-    [packed data, block coordinates] padded to the longest (on NCCL all links
-    carry data at once and nothing leaves HBM but the coordinates); one
-    device concatenation puts the data in packed order.  On gloo (CPU tests)
-    the same steps run on host tensors."""
+    Two collectives: the per-rank lengths, then one all_gather of every
+    rank's [packed data, block coordinates] padded to the longest (on NCCL
+    all links carry data at once and nothing leaves HBM but the
+    coordinates).  Shards hold interleaved subsets of the sorted output
+    block list (contract_shard assigns blocks by longest processing time),
+    so one device concatenation of the received blocks, taken in sorted
+    coordinate order, gives the packed data.  On gloo (CPU tests) the same
+    steps run on host tensors."""
     import torch
     import torch.distributed as dist
 
@@ -369,16 +372,59 @@ def allgather(shard, group=None):
             torch.tensor([x for c in coords for x in c], dtype=torch.int64, device=dev))
     recv = torch.empty(world * pad, dtype=torch.float64, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
-    crd = torch.cat([recv[r * pad + v: r * pad + v + c] for r, (v, c) in enumerate(counts) if c])
-    flat_c = crd.view(torch.int64).tolist() if crd.numel() else []
-    all_coords = [tuple(flat_c[i: i + nd]) for i in range(0, len(flat_c), nd)]
-    parts = [recv[r * pad: r * pad + v] for r, (v, _) in enumerate(counts) if v]
+    # every rank's blocks, as (coords, start in recv, doubles), in rank order
+    blocks = []
+    for r, (v, c) in enumerate(counts):
+        if not c:
+            continue
+        flat_c = recv[r * pad + v: r * pad + v + c].view(torch.int64).tolist()
+        start = r * pad
+        for i in range(0, len(flat_c), nd):
+            crd = tuple(flat_c[i: i + nd])
+            n = width
+            for ax, q in enumerate(crd):
+                n *= sizes[ax][q]
+            blocks.append((crd, start, n))
+            start += n
+    blocks.sort(key=lambda x: x[0])
+    all_coords = [b[0] for b in blocks]
+    # runs of blocks that are adjacent in recv become one slice each
+    parts, run0, run1 = [], None, None
+    for _, st_, n in blocks:
+        if run1 is not None and st_ == run1:
+            run1 += n
+            continue
+        if run1 is not None and run1 > run0:
+            parts.append(recv[run0:run1])
+        run0, run1 = st_, st_ + n
+    if run1 is not None and run1 > run0:
+        parts.append(recv[run0:run1])
     data = torch.cat(parts) if parts else torch.empty(0, dtype=torch.float64, device=dev)
     if nccl:
         torch.cuda.current_stream().synchronize()
         return type(shard).from_torch(sizes, all_coords, data.view(torch.complex128) if width == 2 else data)
     flat = data.numpy()
     return type(shard).from_blocks(sizes, all_coords, flat.view(np.complex128) if width == 2 else flat)
+
+
+def contract_through_diag(a, labels_a, s, labels_s, b, labels_b, rank: int = 0, nranks: int = 1):
+    """(A . S) . B with S a rank-2 DiagBlockSparse between A and B: S's first
+    label is contracted with one axis of A, its second with one axis of B,
+    and every other label of A and B is positive.  The result is
+    contract(contract_diag(A, S), B): the free axes of A and B in label
+    order.  Runs as one grouped launch that scales A's contracted index by
+    S's diagonal while loading A (no A . S intermediate) when S's blocks are
+    square and each coordinate of A's contracted axis meets one S block.
+    rank / nranks: this rank's share of the output blocks (contract_shard's
+    assignment)."""
+    la, na = _labels(labels_a)
+    ls, ns = _labels(labels_s)
+    lb, nb = _labels(labels_b)
+    st = ctypes.c_int(-999)
+    p = a._f("contract_through_diag")(a._ptr, la, na, s._ptr, ls, ns, b._ptr, lb, nb, int(rank), int(nranks),
+                                      ctypes.byref(st))
+    _raise(st.value, "blocksparse contract_through_diag")
+    return type(a)(p)
 
 
 def contract_diag(a, labels_a, s, labels_s):
@@ -392,4 +438,4 @@ def contract_diag(a, labels_a, s, labels_s):
 
 
 __all__ = ["BlockSparseF64", "BlockSparseC64", "DiagBlockSparseF64", "DiagBlockSparseC64", "contract",
-           "contract_shard", "contract_select", "shard_plan", "allgather", "contract_diag"]
+           "contract_shard", "contract_select", "shard_plan", "allgather", "contract_diag", "contract_through_diag"]

@@ -50,9 +50,12 @@ def test_shard_plan_is_flop_balanced(ndt):
         assert sum(blocks) == 489  # every output block in exactly one shard
         assert abs(sum(flops) - total) <= 1e-9 * total
         if n > 1:
-            # contiguous cuts never split a block; the largest output block
-            # bounds the imbalance
-            assert max(flops) <= total / n + max_block_flops((sa, ca), la, (sb, cb), lb) + 1
+            # longest processing time first never splits a block: the
+            # heaviest block bounds both the excess over the mean and the
+            # spread between ranks
+            big = max_block_flops((sa, ca), la, (sb, cb), lb)
+            assert max(flops) <= total / n + big + 1
+            assert max(flops) - min(flops) <= big + 1
 
 
 def max_block_flops(A, la, B, lb):
@@ -70,7 +73,7 @@ def max_block_flops(A, la, B, lb):
     return max(per.values())
 
 
-def _gather_worker(rank, world, port, q, cplx=False):
+def _gather_worker(rank, world, port, q, cplx=False, interleaved=False):
     import sys
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
@@ -91,12 +94,17 @@ def _gather_worker(rank, world, port, q, cplx=False):
         data = np.arange(offs[-1], dtype=float) * 1.5
         if cplx:
             data = data - 0.5j * data[::-1]
-        # contiguous shards of the sorted block list; with 3 ranks the middle
-        # one holds no block (more ranks than output blocks)
-        ranges = [(0, 2), (2, 4)] if world == 2 else [(0, 2), (2, 2), (2, 4)]
-        lo, hi = ranges[rank]
+        # shards of the sorted block list, contiguous or interleaved (as
+        # contract_shard's heaviest-first assignment makes them); with 3
+        # ranks the middle one holds no block (more ranks than output blocks)
+        if world == 2:
+            owned = [[0, 2], [1, 3]] if interleaved else [[0, 1], [2, 3]]
+        else:
+            owned = [[0, 3], [], [1, 2]] if interleaved else [[0, 1], [], [2, 3]]
+        mine = owned[rank]
         cls = ndt.blocksparse.BlockSparseC64 if cplx else ndt.blocksparse.BlockSparseF64
-        shard = cls.from_blocks(sizes, all_coords[lo:hi], data[offs[lo]:offs[hi]])
+        part = np.concatenate([data[offs[i]:offs[i + 1]] for i in mine]) if mine else data[:0]
+        shard = cls.from_blocks(sizes, [all_coords[i] for i in mine], part)
         full = ndt.blocksparse.allgather(shard)
         ok = full.coords == all_coords and np.array_equal(full.to_numpy_data(), data)
         q.put((rank, bool(ok)))
@@ -104,8 +112,9 @@ def _gather_worker(rank, world, port, q, cplx=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,cplx", [(2, False), (3, True)])
-def test_allgather_shards_gloo(world, cplx):
+@pytest.mark.parametrize("world,cplx,interleaved", [(2, False, False), (3, True, False), (2, True, True),
+                                                     (3, False, True)])
+def test_allgather_shards_gloo(world, cplx, interleaved):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
@@ -114,7 +123,7 @@ def test_allgather_shards_gloo(world, cplx):
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    ps = [ctx.Process(target=_gather_worker, args=(r, world, port, q, cplx)) for r in range(world)]
+    ps = [ctx.Process(target=_gather_worker, args=(r, world, port, q, cplx, interleaved)) for r in range(world)]
     for p in ps:
         p.start()
     res = [q.get(timeout=120) for _ in ps]

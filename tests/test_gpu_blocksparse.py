@@ -97,19 +97,34 @@ def test_blocksparse_no_matching_pairs_and_empty(gpu, oracle):
     _check(gpu, oracle, E, [1, -1], B, [-1, 2])
 
 
+def merge_shards(shards):
+    """Blocks of all shards in sorted coordinate order: (coords, packed data)."""
+    items = []
+    for s in shards:
+        _, coords, offs = s._structure()
+        d = s.to_numpy_data()
+        ends = list(offs[1:]) + [len(d)]
+        items += [(c, d[o:e]) for c, o, e in zip(coords, offs, ends)]
+    items.sort(key=lambda x: x[0])
+    data = np.concatenate([x[1] for x in items]) if items else np.zeros(0)
+    return [x[0] for x in items], data
+
+
 @pytest.mark.parametrize("nranks", [2, 3, 4])
 def test_shards_reassemble_full_result(gpu, oracle, nranks):
     (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
     cls = gpu.blocksparse.BlockSparseF64
     A, B = cls.from_blocks(sa, ca, a), cls.from_blocks(sb, cb, b)
     full = gpu.blocksparse.contract(A, la, B, lb)
-    coords, chunks = [], []
-    for r in range(nranks):
-        s = gpu.blocksparse.contract_shard(A, la, B, lb, r, nranks)
-        coords += s.coords
-        chunks.append(s.to_numpy_data())
+    shards = [gpu.blocksparse.contract_shard(A, la, B, lb, r, nranks) for r in range(nranks)]
+    for s in shards:
+        assert s.coords == sorted(s.coords)  # each shard's blocks sorted
+    coords, data = merge_shards(shards)
     assert coords == full.coords
-    assert np.array_equal(np.concatenate(chunks), full.to_numpy_data())  # same kernel, same bits
+    assert np.array_equal(data, full.to_numpy_data())  # same kernel, same bits
+    # heaviest-first assignment: the shards' FLOPs differ by at most one block's
+    blocks, flops = gpu.blocksparse.shard_plan(A, la, B, lb, nranks)
+    assert blocks == [s.nnzblocks for s in shards]
 
 
 def test_cfg4_small_scale_vs_oracle(gpu, oracle):
@@ -214,7 +229,7 @@ def test_cfg5_reduced_bond_chain_vs_oracle(gpu, oracle):
 
 def test_shards_with_more_ranks_than_output_blocks(gpu):
     """Eight ranks over three output blocks: five shards are empty, the rest
-    hold contiguous ranges, and together they are the full result."""
+    hold one block each, and together they are the full result."""
     bs = gpu.blocksparse
     rng = np.random.default_rng(41)
     sizes = [[3, 4, 5], [2, 6]]
@@ -226,9 +241,8 @@ def test_shards_with_more_ranks_than_output_blocks(gpu):
     shards = [bs.contract_shard(A, [1, -1], B, [-1, 2], r, 8) for r in range(8)]
     assert sum(s.nnzblocks for s in shards) == full.nnzblocks == 3
     assert sum(1 for s in shards if s.nnzblocks == 0) == 5
-    coords = [c for s in shards for c in s.coords]
+    coords, data = merge_shards(shards)
     assert coords == full.coords
-    data = np.concatenate([s.to_numpy_data() for s in shards])
     np.testing.assert_array_equal(data, full.to_numpy_data())
     blocks, flops = bs.shard_plan(A, [1, -1], B, [-1, 2], 8)
     assert blocks == [s.nnzblocks for s in shards]
@@ -307,3 +321,96 @@ def test_literal_size_selected_blocks_vs_numpy(gpu):
             ref += da[x].reshape((m, k), order="F") @ db[y].reshape((k, n), order="F")
         blk = got.block(o).reshape((m, n), order="F")
         assert np.linalg.norm(blk - ref) <= 1e-12 * np.linalg.norm(ref)
+
+
+def _through_diag_ref(oracle, A, la, S, ls, B, lb):
+    """Oracle of (A . S) . B: S made dense blocks, then two contract_blocksparse."""
+    P = max([x for x in list(la) + list(lb) if x > 0] + [0]) + 1
+    Sbs = oracle.bs_from_dense(oracle.diag_to_dense(*S), S[0], S[1])
+    st, AS = oracle.bs_contract(oracle.BlockSparse(*A), la, Sbs, [ls[0], P])
+    assert st == 0
+    las = sorted(x for x in la if x != ls[0]) + [ls[1]]
+    st, C = oracle.bs_contract(AS, las, oracle.BlockSparse(*B), lb)
+    assert st == 0
+    return C
+
+
+def test_through_diag_cfg5_reduced_bond(gpu, oracle):
+    """(A . S) . B of the c128 two-site MPS at bond 1024 as one grouped launch
+    (S's diagonal applied to A's loads) vs the oracle's two contractions, and
+    vs the library's two-step path."""
+    A, S, B = cfg5_tensors(bond=1024)
+    bs = gpu.blocksparse
+    gA, gS, gB = bs.BlockSparseC64.from_blocks(*A), bs.DiagBlockSparseC64.from_blocks(*S), bs.BlockSparseC64.from_blocks(*B)
+    n0 = gpu.launch_count()
+    C = bs.contract_through_diag(gA, [1, 2, -1], gS, [-1, -2], gB, [-2, 3, 4])
+    assert gpu.launch_count() - n0 == 1  # one grouped GEMM, no scaling pass
+    ref = _through_diag_ref(oracle, A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4])
+    assert C.coords == ref.coords and C.block_sizes == ref.block_sizes
+    assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
+    two = bs.contract(bs.contract_diag(gA, [1, 2, -1], gS, [-1, 5]), [1, 2, -1], gB, [-1, 3, 4])
+    assert two.coords == C.coords
+    assert rel_fro(C.to_numpy_data(), two.to_numpy_data()) <= RTOL
+    # sharded: every rank's blocks together are the full result, bit for bit
+    for n in (2, 3, 8):
+        shards = [bs.contract_through_diag(gA, [1, 2, -1], gS, [-1, -2], gB, [-2, 3, 4], r, n) for r in range(n)]
+        coords, data = merge_shards(shards)
+        assert coords == C.coords
+        assert np.array_equal(data, C.to_numpy_data())
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+@pytest.mark.parametrize("la,lb", [
+    ([1, 2, -1], [-2, 3]),   # A MN-major, B K-major
+    ([-1, 1, 2], [-2, 3]),   # A K-major
+    ([1, -1], [3, -2]),      # B MN-major
+    ([1, -1, 2], [3, -2, 4]),  # middle axes: both operands packed first
+])
+def test_through_diag_layouts_vs_oracle(gpu, oracle, cplx, la, lb):
+    rng = np.random.default_rng(61)
+    ksz = [2, 3, 5, 4]
+    free = {1: [3, 2], 2: [1, 4], 3: [2, 5], 4: [3, 1]}
+    sa = [ksz if x < 0 else free[x] for x in la]
+    sb = [ksz if x < 0 else free[x] for x in lb]
+    A = random_bs(rng, sa, 0.7, cplx)
+    B = random_bs(rng, sb, 0.7, cplx)
+    scoords = [(0, 0), (1, 1), (3, 3)]  # square diagonal blocks; coordinate 2 has none
+    nd = sum(ksz[c[0]] for c in scoords)
+    diag = rng.standard_normal(nd) + (1j * rng.standard_normal(nd) if cplx else 0)
+    S = ([ksz, ksz], scoords, diag)
+    bs = gpu.blocksparse
+    cls = _cls(gpu, cplx)
+    dcls = bs.DiagBlockSparseC64 if cplx else bs.DiagBlockSparseF64
+    C = bs.contract_through_diag(cls.from_blocks(*A), la, dcls.from_blocks(*S), [-1, -2], cls.from_blocks(*B), lb)
+    ref = _through_diag_ref(oracle, A, la, S, [-1, -2], B, lb)
+    assert C.coords == ref.coords and C.block_sizes == ref.block_sizes
+    assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
+
+
+def test_through_diag_fallbacks_and_errors(gpu, oracle):
+    """Off-diagonal S blocks map A's coordinate q to B's q' (fused); a
+    non-square S block or two S blocks on one coordinate take the two-step
+    path; label misuse is an error."""
+    rng = np.random.default_rng(62)
+    bs = gpu.blocksparse
+    ksz = [3, 3, 2]
+    A = random_bs(rng, [[2, 4], ksz], 0.9, False)
+    B = random_bs(rng, [ksz, [3, 2]], 0.9, False)
+    cls, dcls = bs.BlockSparseF64, bs.DiagBlockSparseF64
+    for scoords in ([(0, 1), (1, 0), (2, 2)],      # permuting square blocks: fused
+                    [(0, 2), (2, 1)],              # non-square (3 vs 2): two-step
+                    [(0, 0), (0, 1)]):             # one coordinate, two blocks: two-step
+        nd = sum(min(ksz[c[0]], ksz[c[1]]) for c in scoords)
+        S = ([ksz, ksz], scoords, rng.standard_normal(nd))
+        C = bs.contract_through_diag(cls.from_blocks(*A), [1, -1], dcls.from_blocks(*S), [-1, -2],
+                                     cls.from_blocks(*B), [-2, 2])
+        ref = _through_diag_ref(oracle, A, [1, -1], S, [-1, -2], B, [-2, 2])
+        assert C.coords == ref.coords
+        assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
+    S = dcls.from_blocks([ksz, ksz], [(0, 0)], np.ones(3))
+    gA, gB = cls.from_blocks(*A), cls.from_blocks(*B)
+    for la, ls, lb in (([1, -1], [-1, 2], [-2, 2]),     # S label not negative
+                       ([1, -3], [-1, -2], [-2, 2]),    # A lacks S's first label
+                       ([1, -1], [-1, -2], [-2, 1])):   # A and B share a label
+        with pytest.raises(gpu.NDTensorsError):
+            bs.contract_through_diag(gA, la, S, ls, gB, lb)
