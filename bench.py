@@ -820,7 +820,7 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
         kept = [(i, c) for i, c in enumerate(coords) if c in keep]
         t = bs.BlockSparseF64.zeros(sizes, [c for _, c in kept])
         if t.nnz:
-            view = torch.as_tensor(bs._DeviceSpan(t.device_ptr(), t.nnz), device="cuda")
+            view = torch.as_tensor(bs._DeviceSpan(t.device_ptr_mut(), t.nnz), device="cuda")
             off = 0
             for i, c in kept:
                 g = torch.Generator(device="cuda").manual_seed(seed * 1000 + i)

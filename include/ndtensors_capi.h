@@ -137,14 +137,18 @@ ndt_tensor_c64* ndt_tensor_c64_contract_gemm(const ndt_tensor_c64* a, const long
 /* Device-pointer interop (the device-pointer ABI proposed in the reference's
  * README, "CUDA support" section).  from_device_ptr copies `len` elements from
  * device memory of the current device; device_ptr returns the tensor's device
- * buffer (valid until mutation / release; work on it is ordered on the
- * library stream). */
+ * buffer for reading (valid until mutation / release; work on it is ordered on
+ * the library stream); device_ptr_mut returns it for writing from outside the
+ * library (copy on write if shared, as data_mut; the device copy then holds
+ * the tensor's values, and host views are refreshed from it). */
 ndt_tensor_f64* ndt_tensor_f64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
                                                int* status);
 const double* ndt_tensor_f64_device_ptr(const ndt_tensor_f64* tensor);
+double* ndt_tensor_f64_device_ptr_mut(ndt_tensor_f64* tensor);
 ndt_tensor_c64* ndt_tensor_c64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
                                                int* status);
 const double* ndt_tensor_c64_device_ptr(const ndt_tensor_c64* tensor);
+double* ndt_tensor_c64_device_ptr_mut(ndt_tensor_c64* tensor);
 
 /* Raw device kernels, no handles, no allocation by the library.
  * dtype: 0 = f64, 1 = complex128.  `stream` is a cudaStream_t; NULL is the
@@ -196,6 +200,15 @@ int ndt_blocksparse_f64_insert_block(ndt_blocksparse_f64* t, const size_t* coord
 int ndt_blocksparse_f64_get_block(const ndt_blocksparse_f64* t, const size_t* coords, double* out, size_t len);
 const double* ndt_blocksparse_f64_data(const ndt_blocksparse_f64* t);       /* host view of packed data */
 const double* ndt_blocksparse_f64_device_ptr(const ndt_blocksparse_f64* t); /* device view of packed data */
+double* ndt_blocksparse_f64_device_ptr_mut(ndt_blocksparse_f64* t); /* for writing (as the dense device_ptr_mut) */
+/* A tensor from blocks lying anywhere in device memory (no counterpart in the reference): block i of
+ * the listed structure is read at src + src_offsets[i] elements (each block inside [0, src_len)); the
+ * result stores the blocks sorted by coordinates, packed, written by one copy kernel.  Assembles the
+ * shards of a sharded contraction gathered into one buffer. */
+ndt_blocksparse_f64* ndt_blocksparse_f64_from_device_blocks(size_t ndim, const size_t* nblocks,
+                                                            const size_t* block_sizes, size_t nnzb,
+                                                            const size_t* coords, const size_t* src_offsets,
+                                                            const double* src, size_t src_len, int* status);
 /* contract_blocksparse (contract/blocksparse.rs:87-183): one grouped FP64 tensor-core launch */
 ndt_blocksparse_f64* ndt_blocksparse_f64_contract(const ndt_blocksparse_f64* a, const long* labels_a,
                                                   size_t ndim_a, const ndt_blocksparse_f64* b, const long* labels_b,
@@ -218,6 +231,14 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_contract_select(const ndt_blocksparse_c
                                                          size_t ndim_a, const ndt_blocksparse_c64* b,
                                                          const long* labels_b, size_t ndim_b,
                                                          const size_t* out_coords, size_t nout, int* status);
+/* Which rank holds which output block, for a shard returned by contract_shard / contract_through_diag
+ * with nranks > 1 (NDT_INVALID_ARGUMENT for any other tensor): *nranks, *nblocks (all output blocks),
+ * then, when the arrays are not NULL, the blocks' coordinates (nblocks x ndim, sorted) and owners.
+ * Every rank gets the same layout, so shards can be gathered without exchanging their structure. */
+int ndt_blocksparse_f64_shard_layout(const ndt_blocksparse_f64* t, int* nranks, size_t* nblocks, size_t* coords,
+                                     int* owners);
+int ndt_blocksparse_c64_shard_layout(const ndt_blocksparse_c64* t, int* nranks, size_t* nblocks, size_t* coords,
+                                     int* owners);
 /* Host-only plan of contract_shard: output blocks and real flops per rank (either array may be NULL) */
 int ndt_blocksparse_f64_shard_plan(const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a,
                                    const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b, int nranks,
@@ -255,6 +276,11 @@ int ndt_blocksparse_c64_insert_block(ndt_blocksparse_c64* t, const size_t* coord
 int ndt_blocksparse_c64_get_block(const ndt_blocksparse_c64* t, const size_t* coords, double* out, size_t len);
 const double* ndt_blocksparse_c64_data(const ndt_blocksparse_c64* t);
 const double* ndt_blocksparse_c64_device_ptr(const ndt_blocksparse_c64* t);
+double* ndt_blocksparse_c64_device_ptr_mut(ndt_blocksparse_c64* t);
+ndt_blocksparse_c64* ndt_blocksparse_c64_from_device_blocks(size_t ndim, const size_t* nblocks,
+                                                            const size_t* block_sizes, size_t nnzb,
+                                                            const size_t* coords, const size_t* src_offsets,
+                                                            const double* src, size_t src_len, int* status);
 ndt_blocksparse_c64* ndt_blocksparse_c64_contract(const ndt_blocksparse_c64* a, const long* labels_a,
                                                   size_t ndim_a, const ndt_blocksparse_c64* b, const long* labels_b,
                                                   size_t ndim_b, int* status);

@@ -28,12 +28,22 @@
 
 namespace ndt {
 
+// Which rank holds which output block of a sharded contraction: every rank
+// derives the same layout, so the shards can be gathered without exchanging
+// their structure.
+struct ShardLayout {
+  int nranks = 1;
+  std::vector<std::vector<size_t>> coords;  // all output blocks, sorted
+  std::vector<int> owner;                   // rank holding each of them
+};
+
 struct BlockSparseT {
   DType dt = DType::F64;
   std::vector<std::vector<size_t>> bsz;     // per-axis block sizes
   std::vector<std::vector<size_t>> coords;  // stored blocks, storage order
   std::vector<size_t> offs;                 // packed offsets, size nnzb + 1
   std::shared_ptr<Storage> st;
+  std::shared_ptr<const ShardLayout> layout;  // set on the shards of a sharded contraction
 
   size_t ndim() const { return bsz.size(); }
   size_t nnzb() const { return coords.size(); }
@@ -316,6 +326,13 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   }
   for (size_t i = 0; i < all_out.size(); i++)
     if (owner[i] == rank) C.coords.push_back(all_out[i]);
+  if (nranks > 1) {
+    auto lay = std::make_shared<ShardLayout>();
+    lay->nranks = nranks;
+    lay->coords = all_out;
+    lay->owner = owner;
+    C.layout = lay;
+  }
   C.pack();
   C.st = std::make_shared<Storage>(C.dt, C.total());
   if (C.total() == 0 || contrib.empty()) {
@@ -737,6 +754,35 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
   return bs_contract(AS, las, B, lb, rank, nranks);
 }
 
+// A block-sparse tensor from blocks lying anywhere in device memory: block i
+// of `cs` is read at src + src_off[i] elements; the result holds the blocks
+// sorted by coordinates, packed (as contract_blocksparse orders its output),
+// written by one segmented copy.  Assembles gathered shards.
+BlockSparseT bs_from_device_blocks(DType dt, const std::vector<std::vector<size_t>>& bsz,
+                                   const std::vector<std::vector<size_t>>& cs, const size_t* src_off,
+                                   const void* src, size_t src_len) {
+  std::vector<size_t> order(cs.size());
+  for (size_t i = 0; i < order.size(); i++) order[i] = i;
+  std::sort(order.begin(), order.end(), [&](size_t x, size_t y) { return cs[x] < cs[y]; });
+  std::vector<std::vector<size_t>> sorted;
+  for (size_t i : order) sorted.push_back(cs[i]);
+  BlockSparseT t = make_bs(dt, bsz, sorted);
+  if (t.total() == 0) return t;
+  const size_t es = esize(dt);
+  std::vector<int64_t> so, dso, nb;
+  for (size_t r = 0; r < order.size(); r++) {
+    const size_t n = t.block_elems(t.coords[r]);
+    const size_t o = src_off[order[r]];
+    if (o > src_len || n > src_len - o) throw Error(ErrKind::ShapeMismatch, "block outside the source range");
+    so.push_back((int64_t)(o * es));
+    dso.push_back((int64_t)(t.offs[r] * es));
+    nb.push_back((int64_t)(n * es));
+  }
+  void* d = t.st->dev_overwrite();
+  copy_segments(src, d, so, dso, nb, ctx().compute);
+  return t;
+}
+
 }  // namespace ndt
 
 // =========================================================================
@@ -923,6 +969,30 @@ extern "C" {
       return new NdtBs{t};                                                                                           \
     });                                                                                                              \
   }                                                                                                                  \
+  T* ndt_blocksparse_##DT##_from_device_blocks(size_t ndim, const size_t* nblocks, const size_t* block_sizes,        \
+                                               size_t nnzb, const size_t* coords, const size_t* src_offsets,         \
+                                               const double* src, size_t src_len, int* status) {                    \
+    return (T*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                  \
+      if (nnzb && (!src || !src_offsets)) throw Error(ErrKind::InvalidArgument, "NULL device pointer or offsets");   \
+      std::vector<std::vector<size_t>> bsz, cs;                                                                      \
+      read_structure(ndim, nblocks, block_sizes, nnzb, coords, &bsz, &cs);                                           \
+      return new NdtBs{bs_from_device_blocks(DTYPE_##DT, bsz, cs, src_offsets, src, src_len)};                       \
+    });                                                                                                              \
+  }                                                                                                                  \
+  int ndt_blocksparse_##DT##_shard_layout(const T* t, int* nranks, size_t* nblocks, size_t* coords, int* owners) {   \
+    if (!t || !nranks || !nblocks) return NDT_INVALID_ARGUMENT;                                                      \
+    const BlockSparseT& b = ((const NdtBs*)t)->t;                                                                    \
+    if (!b.layout) return NDT_INVALID_ARGUMENT;                                                                      \
+    *nranks = b.layout->nranks;                                                                                      \
+    *nblocks = b.layout->coords.size();                                                                              \
+    const size_t nd = b.ndim();                                                                                      \
+    for (size_t i = 0; i < b.layout->coords.size(); i++) {                                                           \
+      if (coords)                                                                                                    \
+        for (size_t a = 0; a < nd; a++) coords[i * nd + a] = b.layout->coords[i][a];                                 \
+      if (owners) owners[i] = b.layout->owner[i];                                                                    \
+    }                                                                                                                \
+    return NDT_SUCCESS;                                                                                              \
+  }                                                                                                                  \
   void ndt_blocksparse_##DT##_release(T* t) { delete (NdtBs*)t; }                                                    \
   size_t ndt_blocksparse_##DT##_ndim(const T* t) { return t ? ((const NdtBs*)t)->t.ndim() : 0; }                     \
   size_t ndt_blocksparse_##DT##_nnzblocks(const T* t) { return t ? ((const NdtBs*)t)->t.nnzb() : 0; }                \
@@ -956,6 +1026,17 @@ extern "C" {
     if (!t) return nullptr;                                                                                          \
     try {                                                                                                            \
       return (const double*)((const NdtBs*)t)->t.st->dev_read();                                                     \
+    } catch (const std::exception& e) {                                                                              \
+      set_last_error(e.what());                                                                                      \
+      return nullptr;                                                                                                \
+    }                                                                                                                \
+  }                                                                                                                  \
+  double* ndt_blocksparse_##DT##_device_ptr_mut(T* t) {                                                              \
+    if (!t) return nullptr;                                                                                          \
+    try {                                                                                                            \
+      BlockSparseT& b = ((NdtBs*)t)->t;                                                                              \
+      if (b.st.use_count() > 1) b.st = b.st->clone(); /* copy on write */                                            \
+      return (double*)b.st->dev_write();                                                                             \
     } catch (const std::exception& e) {                                                                              \
       set_last_error(e.what());                                                                                      \
       return nullptr;                                                                                                \

@@ -10,6 +10,11 @@
 //   bs_diag_scale     out block = A block with its last axis scaled by the
 //                     diagonal of the matching diag block (the fused
 //                     block-sparse x diag-block-sparse contraction).
+//   copy_segments     many (src, dst, bytes) copies in one launch: 64 KB
+//                     work items, the segment found by binary search over
+//                     the items' prefix, 16-byte vectors where a segment's
+//                     addresses and length allow (assembling gathered shards
+//                     into sorted block order).
 #include <algorithm>
 #include <cstring>
 
@@ -134,7 +139,64 @@ Tables upload(const std::vector<int64_t>& offs, const std::vector<BsBlockDesc>& 
   NDT_CUDA(cudaMemcpyAsync(d, h.data(), total, cudaMemcpyHostToDevice, s));
   return Tables{(int64_t*)d, (BsBlockDesc*)((char*)d + o2), d};
 }
+constexpr int64_t kSegChunk = 65536;  // bytes per work item
+
+struct CopySeg {
+  int64_t src, dst, bytes;  // byte offsets and length
+  int64_t item0;            // first work item of the segment
+};
+
+__global__ void __launch_bounds__(kThreads) copy_segments_kernel(const char* __restrict__ src, char* __restrict__ dst,
+                                                                 const CopySeg* __restrict__ segs, int nseg,
+                                                                 int64_t nitems) {
+  for (int64_t it = blockIdx.x; it < nitems; it += gridDim.x) {
+    int lo = 0, hi = nseg - 1;  // segs[s].item0 <= it < segs[s+1].item0
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (segs[mid].item0 <= it)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    const CopySeg sg = segs[lo];
+    const int64_t b0 = (it - sg.item0) * kSegChunk;
+    const int64_t b1 = min(b0 + kSegChunk, sg.bytes);
+    const char* sp = src + sg.src;
+    char* dp = dst + sg.dst;
+    if (((sg.src | sg.dst | sg.bytes) & 15) == 0) {
+      for (int64_t b = b0 + threadIdx.x * 16; b < b1; b += kThreads * 16)
+        *reinterpret_cast<int4*>(dp + b) = *reinterpret_cast<const int4*>(sp + b);
+    } else {
+      for (int64_t b = b0 + threadIdx.x * 8; b < b1; b += kThreads * 8)
+        *reinterpret_cast<double*>(dp + b) = *reinterpret_cast<const double*>(sp + b);
+    }
+  }
+}
 }  // namespace
+
+void copy_segments(const void* src, void* dst, const std::vector<int64_t>& src_off, const std::vector<int64_t>& dst_off,
+                   const std::vector<int64_t>& bytes, cudaStream_t s) {
+  std::vector<CopySeg> h;
+  int64_t items = 0;
+  for (size_t i = 0; i < bytes.size(); i++) {
+    if (bytes[i] <= 0) continue;
+    if ((src_off[i] | dst_off[i] | bytes[i]) & 7) throw Error(ErrKind::Panic, "copy_segments: not 8-byte aligned");
+    h.push_back(CopySeg{src_off[i], dst_off[i], bytes[i], items});
+    items += (bytes[i] + kSegChunk - 1) / kSegChunk;
+  }
+  if (h.empty()) return;
+  if ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) throw Error(ErrKind::Panic, "copy_segments: base not 16-byte aligned");
+  CopySeg* d = nullptr;
+  const size_t tb = h.size() * sizeof(CopySeg);
+  NDT_CUDA(cudaMallocAsync((void**)&d, tb, s));
+  NDT_CUDA(cudaMemcpyAsync(d, h.data(), tb, cudaMemcpyHostToDevice, s));
+  const DeviceCtx& c = ctx();
+  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, (int64_t)c.sm_count * 8));
+  copy_segments_kernel<<<grid, kThreads, 0, s>>>((const char*)src, (char*)dst, d, (int)h.size(), items);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+  NDT_CUDA(cudaFreeAsync(d, s));
+}
 
 void bs_dense_map(DType dt, void* packed, void* dense, const std::vector<int64_t>& offs,
                   const std::vector<BsBlockDesc>& blocks, int64_t total, bool to_dense, cudaStream_t s) {

@@ -313,6 +313,18 @@ const double* device_ptr_impl(const void* t) {
   }
 }
 
+double* device_ptr_mut_impl(void* t) {
+  if (!t) return nullptr;
+  try {
+    Dense& d = H(t)->t;
+    d.make_unique();  // copy on write, as data_mut
+    return (double*)d.st->dev_write();
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    return nullptr;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -509,11 +521,13 @@ ndt_tensor_f64* ndt_tensor_f64_from_device_ptr(const double* dptr, size_t len, c
   return (ndt_tensor_f64*)from_device_impl(DType::F64, dptr, len, shape, ndim, status);
 }
 const double* ndt_tensor_f64_device_ptr(const ndt_tensor_f64* t) { return device_ptr_impl(t); }
+double* ndt_tensor_f64_device_ptr_mut(ndt_tensor_f64* t) { return device_ptr_mut_impl(t); }
 ndt_tensor_c64* ndt_tensor_c64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
                                                int* status) {
   return (ndt_tensor_c64*)from_device_impl(DType::C128, dptr, len, shape, ndim, status);
 }
 const double* ndt_tensor_c64_device_ptr(const ndt_tensor_c64* t) { return device_ptr_impl(t); }
+double* ndt_tensor_c64_device_ptr_mut(ndt_tensor_c64* t) { return device_ptr_mut_impl(t); }
 
 int ndt_b200_permutedims_dev(int dtype, const void* src, void* dst, const size_t* shape, size_t ndim,
                              const size_t* perm, size_t nperm, void* stream) {

@@ -132,6 +132,9 @@ struct Storage {
   const void* dev_read();
   // Device view for a kernel that overwrites every element.
   void* dev_overwrite();
+  // Device view for writes from outside the library (any subset of the
+  // elements): materialised, then the device copy is the only valid one.
+  void* dev_write();
   void set_uniform(double re, double im);
   std::shared_ptr<Storage> clone() const;
 };
@@ -259,6 +262,10 @@ void diag_scatter(DType dt, const void* diag, void* out, const std::vector<int64
                   const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s);
 void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const std::vector<int64_t>& offs,
                    const std::vector<BsBlockDesc>& blocks, int64_t total, cudaStream_t s);
+// Byte ranges src + src_off[i] -> dst + dst_off[i] (bytes[i] long, all
+// multiples of 8; bases 16-byte aligned) in one launch.
+void copy_segments(const void* src, void* dst, const std::vector<int64_t>& src_off, const std::vector<int64_t>& dst_off,
+                   const std::vector<int64_t>& bytes, cudaStream_t s);
 
 // Elementwise helpers
 void fill_device(DType dt, void* p, size_t n, double re, double im, cudaStream_t s);

@@ -122,6 +122,13 @@ void* Storage::dev_overwrite() {
   return dev;
 }
 
+void* Storage::dev_write() {
+  void* p = const_cast<void*>(dev_read());
+  uniform = false;
+  host_valid = false;
+  return p;
+}
+
 void Storage::set_uniform(double re, double im) {
   uniform = true;
   fill_re = re;

@@ -80,8 +80,10 @@ SIGNATURES = [
     ("ndt_tensor_c64_contract_gemm", vp, [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
     ("ndt_tensor_f64_from_device_ptr", vp, [vp, ctypes.c_size_t, c_size_p, ctypes.c_size_t, c_int_p]),
     ("ndt_tensor_f64_device_ptr", vp, [vp]),
+    ("ndt_tensor_f64_device_ptr_mut", vp, [vp]),
     ("ndt_tensor_c64_from_device_ptr", vp, [vp, ctypes.c_size_t, c_size_p, ctypes.c_size_t, c_int_p]),
     ("ndt_tensor_c64_device_ptr", vp, [vp]),
+    ("ndt_tensor_c64_device_ptr_mut", vp, [vp]),
     (
         "ndt_b200_permutedims_dev",
         ctypes.c_int,
@@ -112,6 +114,11 @@ SIGNATURES = [
             (f"ndt_blocksparse_{dt}_get_block", ctypes.c_int, [vp, c_size_p, c_double_p, ctypes.c_size_t]),
             (f"ndt_blocksparse_{dt}_data", c_double_p, [vp]),
             (f"ndt_blocksparse_{dt}_device_ptr", vp, [vp]),
+            (f"ndt_blocksparse_{dt}_device_ptr_mut", vp, [vp]),
+            (f"ndt_blocksparse_{dt}_shard_layout", ctypes.c_int,
+             [vp, c_int_p, c_size_p, c_size_p, c_int_p]),
+            (f"ndt_blocksparse_{dt}_from_device_blocks", vp,
+             [ctypes.c_size_t, c_size_p, c_size_p, ctypes.c_size_t, c_size_p, c_size_p, vp, ctypes.c_size_t, c_int_p]),
             (f"ndt_blocksparse_{dt}_contract", vp,
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, c_int_p]),
             (f"ndt_blocksparse_{dt}_contract_shard", vp,

@@ -90,8 +90,56 @@ class _BsBase:
         _raise(st.value, "blocksparse from_device_ptr")
         return cls(p)
 
+    @classmethod
+    def from_device_blocks(cls, block_sizes, coords, src_offsets, src_ptr: int, src_len: int):
+        """Blocks read from anywhere in device memory: block i of `coords` at
+        element offset src_offsets[i] of the buffer at src_ptr (src_len
+        elements); the result holds them sorted by coordinates, packed (one
+        copy kernel)."""
+        if isinstance(coords, np.ndarray):  # n x ndim array: no per-block Python objects
+            ndim = len(block_sizes)
+            flat = [int(x) for b in block_sizes for x in b]
+            nblk = (SZ * max(ndim, 1))(*[len(b) for b in block_sizes])
+            bsz = (SZ * max(len(flat), 1))(*flat)
+            carr = np.ascontiguousarray(coords, dtype=np.uint64).ravel()
+            nnzb = coords.shape[0]
+            cs = carr.ctypes.data_as(ctypes.POINTER(SZ)) if carr.size else (SZ * 1)()
+        else:
+            ndim, nblk, bsz, nnzb, cs = _structure_args(block_sizes, coords)
+        offs = np.ascontiguousarray(np.asarray(src_offsets, dtype=np.uint64))
+        op = offs.ctypes.data_as(ctypes.POINTER(SZ)) if offs.size else (SZ * 1)()
+        st = ctypes.c_int(-999)
+        p = getattr(get_lib(), f"ndt_blocksparse_{cls._prefix}_from_device_blocks")(
+            ndim, nblk, bsz, nnzb, cs, op, ctypes.c_void_p(int(src_ptr)), int(src_len), ctypes.byref(st))
+        _raise(st.value, "blocksparse from_device_blocks")
+        return cls(p)
+
+    def _shard_layout(self):
+        """(nranks, all output block coordinates (n x ndim, sorted), owner
+        rank of each) for a shard of a sharded contraction, else None."""
+        nr, nb = ctypes.c_int(0), SZ(0)
+        if self._f("shard_layout")(self._ptr, ctypes.byref(nr), ctypes.byref(nb), None, None) != 0:
+            return None
+        nd = max(self.ndim, 1)
+        crd = np.zeros(max(nb.value * nd, 1), dtype=np.uint64)
+        own = np.zeros(max(nb.value, 1), dtype=np.int32)
+        st = self._f("shard_layout")(self._ptr, ctypes.byref(nr), ctypes.byref(nb),
+                                     crd.ctypes.data_as(ctypes.POINTER(SZ)),
+                                     own.ctypes.data_as(ctypes.POINTER(ctypes.c_int)))
+        check_status(st, "shard_layout")
+        return nr.value, crd[: nb.value * nd].reshape(nb.value, nd).astype(np.int64), own[: nb.value]
+
     def device_ptr(self) -> int:
         return self._f("device_ptr")(self._ptr)
+
+    def device_ptr_mut(self) -> int:
+        """Device buffer of the packed data for writing from outside the
+        library (copy on write if shared; the device copy then holds the
+        values)."""
+        p = self._f("device_ptr_mut")(self._ptr)
+        if not p:
+            raise NDTensorsError(f"device_ptr_mut: {last_error()}")
+        return p
 
     @classmethod
     def from_dense(cls, dense, block_sizes, coords):
@@ -327,19 +375,38 @@ class _DeviceSpan:
                                          "strides": None, "version": 2}
 
 
+_HOST_GROUPS = {}
+
+
+def _host_group(group, dist):
+    """A gloo group over the same ranks as `group` (created once, collectively
+    on first use): host-side exchanges that must not queue behind the
+    device collectives of the NCCL group."""
+    key = id(group) if group is not None else None
+    g = _HOST_GROUPS.get(key)
+    if g is None:
+        ranks = dist.get_process_group_ranks(group) if group is not None else list(range(dist.get_world_size()))
+        g = _HOST_GROUPS[key] = dist.new_group(ranks=ranks, backend="gloo")
+    return g
+
+
 def allgather(shard, group=None):
     """Gather every rank's shard (disjoint output blocks of one contraction)
     into the full block-sparse tensor on all ranks, with torch.distributed.
     Blocks come out sorted, as contract_blocksparse orders them.
 
-    Two collectives: the per-rank lengths, then one all_gather of every
-    rank's [packed data, block coordinates] padded to the longest (on NCCL
-    all links carry data at once and nothing leaves HBM but the
-    coordinates).  Shards hold interleaved subsets of the sorted output
-    block list (contract_shard assigns blocks by longest processing time),
-    so one device concatenation of the received blocks, taken in sorted
-    coordinate order, gives the packed data.  On gloo (CPU tests) the same
-    steps run on host tensors."""
+    The layout (which rank holds which blocks) comes with the shards of a
+    sharded contraction (contract_shard, contract_through_diag): every rank
+    derived the same assignment, so nothing is exchanged.  Other shards
+    exchange their structure (packed length, block count, block
+    coordinates) in one small all_gather over host memory; with NCCL it runs
+    on a gloo group over the same ranks, so it neither waits for the kernel
+    still computing the shard nor queues behind device collectives.  Then one
+    all_gather moves every rank's packed data, padded to the longest, over
+    NVLink, and the library assembles the sorted tensor from the gathered
+    buffer with one copy kernel (from_device_blocks).  Nothing on the host
+    waits for the device.  On gloo (CPU tests) the same steps run on host
+    tensors."""
     import torch
     import torch.distributed as dist
 
@@ -347,64 +414,88 @@ def allgather(shard, group=None):
     nccl = dist.get_backend(group) == "nccl"
     dev = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
     sizes, coords, _ = shard._structure()
-    nd = len(sizes)
+    nd = max(len(sizes), 1)
     width = shard._width
-    nelem = shard.nnz
-    nval = nelem * width                      # doubles of packed data
-    ncrd = len(coords) * nd                   # int64 coordinates
-    meta = torch.tensor([nval, ncrd], dtype=torch.int64, device=dev)
-    metas = torch.empty(world * 2, dtype=torch.int64, device=dev)
-    dist.all_gather_into_tensor(metas, meta, group=group)
-    counts = metas.view(world, 2).tolist()
-    pad = max(max(v + c for v, c in counts), 1)
+    nval = shard.nnz * width  # doubles of packed data
+    cap = 1
+    for b in sizes:
+        cap *= max(len(b), 1)
+
+    # ---- structure: [packed length, block count, coordinates...] of every rank
+    def exchange(cpad):
+        mine = np.zeros(2 + cpad * nd, dtype=np.int64)
+        mine[0], mine[1] = nval, len(coords)
+        if coords:
+            mine[2: 2 + len(coords) * nd] = np.asarray(coords, dtype=np.int64).ravel()
+        outs = [torch.empty(mine.size, dtype=torch.int64) for _ in range(world)]
+        dist.all_gather(outs, torch.from_numpy(mine), group=hg)
+        return torch.stack(outs).numpy()
+
+    size_arr = [np.asarray(b, dtype=np.int64) for b in sizes]
+
+    def elems_of(cr):
+        e = np.ones(cr.shape[0], dtype=np.int64)
+        for ax in range(len(sizes)):
+            e *= size_arr[ax][cr[:, ax]]
+        return e
+
+    # every rank's blocks (each shard stores its blocks sorted) and packed length
+    layout = shard._shard_layout()
+    hg = (_host_group(group, dist) if nccl else group) if layout is None or layout[0] != world else None
+    if layout is not None and layout[0] == world:
+        # a shard of a sharded contraction: every rank knows the whole layout
+        _, lc, lo = layout
+        per_rank = [lc[lo == r] for r in range(world)]
+        nvals = [int(elems_of(cr).sum()) * width for cr in per_rank]
+    else:
+        if cap * nd <= (1 << 19):
+            table = exchange(cap)
+        else:  # very many possible blocks: block counts first, then coordinates
+            cnts = [torch.empty(1, dtype=torch.int64) for _ in range(world)]
+            dist.all_gather(cnts, torch.tensor([len(coords)], dtype=torch.int64), group=hg)
+            table = exchange(max(int(max(c.item() for c in cnts)), 1))
+        nvals = [int(v) for v in table[:, 0]]
+        per_rank = [table[r, 2: 2 + int(table[r, 1]) * nd].reshape(int(table[r, 1]), nd) for r in range(world)]
+    # element offsets in the gathered buffer (rank r's data starts at r * pad doubles)
+    pad = max(max(nvals), 1)
+    pad += pad % width  # whole elements per rank
+    all_c, all_off = [], []
+    for r, cr in enumerate(per_rank):
+        if not cr.shape[0]:
+            continue
+        e = elems_of(cr)
+        all_c.append(cr)
+        all_off.append(r * (pad // width) + np.concatenate(([0], np.cumsum(e)[:-1])))
+    gathered_c = np.concatenate(all_c) if all_c else np.zeros((0, nd), dtype=np.int64)
+    gathered_off = np.concatenate(all_off) if all_off else np.zeros(0, dtype=np.int64)
+
+    # ---- data: one all_gather of the packed shards, padded to the longest
+    if nccl and get_lib().ndt_b200_get_stream() != torch.cuda.current_stream().cuda_stream:
+        check_status(get_lib().ndt_b200_synchronize(), "synchronize")  # shard written on another stream
     send = torch.empty(pad, dtype=torch.float64, device=dev)
     if nval:
         if nccl:
-            # the shard was written on the library's stream
-            if get_lib().ndt_b200_get_stream() != torch.cuda.current_stream().cuda_stream:
-                check_status(get_lib().ndt_b200_synchronize(), "synchronize")
             own = torch.as_tensor(_DeviceSpan(shard.device_ptr(), nval), device=dev)
         else:
             own = torch.from_numpy(np.ascontiguousarray(shard.to_numpy_data()).view(np.float64))
         send[:nval].copy_(own)
-    if ncrd:
-        send[nval: nval + ncrd].view(torch.int64).copy_(
-            torch.tensor([x for c in coords for x in c], dtype=torch.int64, device=dev))
     recv = torch.empty(world * pad, dtype=torch.float64, device=dev)
     dist.all_gather_into_tensor(recv, send, group=group)
-    # every rank's blocks, as (coords, start in recv, doubles), in rank order
-    blocks = []
-    for r, (v, c) in enumerate(counts):
-        if not c:
-            continue
-        flat_c = recv[r * pad + v: r * pad + v + c].view(torch.int64).tolist()
-        start = r * pad
-        for i in range(0, len(flat_c), nd):
-            crd = tuple(flat_c[i: i + nd])
-            n = width
-            for ax, q in enumerate(crd):
-                n *= sizes[ax][q]
-            blocks.append((crd, start, n))
-            start += n
-    blocks.sort(key=lambda x: x[0])
-    all_coords = [b[0] for b in blocks]
-    # runs of blocks that are adjacent in recv become one slice each
-    parts, run0, run1 = [], None, None
-    for _, st_, n in blocks:
-        if run1 is not None and st_ == run1:
-            run1 += n
-            continue
-        if run1 is not None and run1 > run0:
-            parts.append(recv[run0:run1])
-        run0, run1 = st_, st_ + n
-    if run1 is not None and run1 > run0:
-        parts.append(recv[run0:run1])
-    data = torch.cat(parts) if parts else torch.empty(0, dtype=torch.float64, device=dev)
-    if nccl:
-        torch.cuda.current_stream().synchronize()
-        return type(shard).from_torch(sizes, all_coords, data.view(torch.complex128) if width == 2 else data)
-    flat = data.numpy()
-    return type(shard).from_blocks(sizes, all_coords, flat.view(np.complex128) if width == 2 else flat)
+    if not nccl:
+        coord_list = [tuple(int(x) for x in row) for row in gathered_c] if len(sizes) else [() for _ in gathered_c]
+        flat = recv.numpy().view(np.complex128) if width == 2 else recv.numpy()
+        parts = [flat[o: o + int(np.prod([sizes[a][q] for a, q in enumerate(c)]))]
+                 for c, o in zip(coord_list, gathered_off)]
+        order = sorted(range(len(coord_list)), key=lambda i: coord_list[i])
+        data = np.concatenate([parts[i] for i in order]) if order else flat[:0]
+        return type(shard).from_blocks(sizes, [coord_list[i] for i in order], data)
+    lib_stream = get_lib().ndt_b200_get_stream()
+    if lib_stream != torch.cuda.current_stream().cuda_stream:
+        torch.cuda.current_stream().synchronize()  # the library reads recv on its own stream
+    out = type(shard).from_device_blocks(sizes, gathered_c, gathered_off, recv.data_ptr(), recv.numel() // width)
+    if lib_stream != torch.cuda.current_stream().cuda_stream:
+        check_status(get_lib().ndt_b200_synchronize(), "synchronize")  # before recv goes back to torch
+    return out
 
 
 def contract_through_diag(a, labels_a, s, labels_s, b, labels_b, rank: int = 0, nranks: int = 1):

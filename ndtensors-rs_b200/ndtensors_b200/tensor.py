@@ -125,6 +125,15 @@ class _DenseBase:
             raise NDTensorsError(f"device_ptr: {last_error()}")
         return p
 
+    def device_ptr_mut(self) -> int:
+        """Device buffer for writing from outside the library (torch, another
+        kernel): copy on write if the storage is shared; the device copy
+        then holds the tensor's values."""
+        p = self._f("device_ptr_mut")(self._ptr)
+        if not p:
+            raise NDTensorsError(f"device_ptr_mut: {last_error()}")
+        return p
+
     @property
     def ndim(self) -> int:
         if self._shape is not None:

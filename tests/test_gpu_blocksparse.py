@@ -125,6 +125,14 @@ def test_shards_reassemble_full_result(gpu, oracle, nranks):
     # heaviest-first assignment: the shards' FLOPs differ by at most one block's
     blocks, flops = gpu.blocksparse.shard_plan(A, la, B, lb, nranks)
     assert blocks == [s.nnzblocks for s in shards]
+    # every shard carries the same layout: all output blocks and their owners
+    lays = [s._shard_layout() for s in shards]
+    for n, lc, lo in lays:
+        assert n == nranks and [tuple(int(x) for x in c) for c in lc] == full.coords
+        assert np.array_equal(lo, lays[0][2])
+    for r, s in enumerate(shards):
+        assert [tuple(int(x) for x in c) for c in lays[0][1][lays[0][2] == r]] == s.coords
+    assert full._shard_layout() is None  # an unsharded result has none
 
 
 def test_cfg4_small_scale_vs_oracle(gpu, oracle):
@@ -414,3 +422,37 @@ def test_through_diag_fallbacks_and_errors(gpu, oracle):
                        ([1, -1], [-1, -2], [-2, 1])):   # A and B share a label
         with pytest.raises(gpu.NDTensorsError):
             bs.contract_through_diag(gA, la, S, ls, gB, lb)
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+def test_from_device_blocks_sorts_and_packs(gpu, cplx):
+    """Blocks scattered in a device buffer (any order, gaps between them)
+    become a tensor with sorted, packed blocks, in one copy launch; a block
+    reaching past the buffer is rejected."""
+    import torch
+
+    rng = np.random.default_rng(71)
+    sizes = [[3, 1, 4], [2, 5]]
+    coords = [(2, 1), (0, 0), (1, 1), (2, 0)]
+    shapes = [(sizes[0][c[0]], sizes[1][c[1]]) for c in coords]
+    blocks = [rng.standard_normal(int(np.prod(sh))) + (1j * rng.standard_normal(int(np.prod(sh))) if cplx else 0)
+              for sh in shapes]
+    dt = np.complex128 if cplx else np.float64
+    offs, buf, pos = [], [], 0
+    for b in blocks:
+        pos += 3  # a gap before every block
+        offs.append(pos)
+        buf += [np.zeros(3, dtype=dt), b.astype(dt)]
+        pos += b.size
+    host = np.concatenate(buf)
+    width = 2 if cplx else 1
+    dbuf = torch.from_numpy(host.view(np.float64).copy()).cuda()
+    cls = _cls(gpu, cplx)
+    n0 = gpu.launch_count()
+    t = cls.from_device_blocks(sizes, coords, offs, dbuf.data_ptr(), dbuf.numel() // width)
+    assert gpu.launch_count() - n0 == 1
+    order = sorted(range(len(coords)), key=lambda i: coords[i])
+    assert t.coords == [coords[i] for i in order]
+    assert np.array_equal(t.to_numpy_data(), np.concatenate([blocks[i].astype(dt) for i in order]))
+    with pytest.raises(ValueError):
+        cls.from_device_blocks(sizes, coords[:1], [pos - 1], dbuf.data_ptr(), dbuf.numel() // width)

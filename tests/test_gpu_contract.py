@@ -180,3 +180,32 @@ def test_torch_interop_device_roundtrip(gpu):
     t = gpu.TensorF64.from_torch(x)
     assert t.shape == (5, 6, 7)
     np.testing.assert_array_equal(t.to_numpy(), x.cpu().numpy())
+
+
+def test_device_ptr_mut_writes_are_the_tensor(gpu):
+    """Writes through device_ptr_mut become the tensor's values: a zeros
+    tensor (held as a uniform value until materialised) filled by torch reads
+    back the written data on the host and in a contraction, and a clone that
+    shared the storage keeps its old values (copy on write)."""
+    import torch
+
+    from ndtensors_b200.blocksparse import _DeviceSpan
+
+    t = gpu.TensorF64.zeros((4, 3))
+    t.device_ptr()  # materialised zeros, storage shared with the clone below
+    keep = gpu.TensorF64(gpu.get_lib().ndt_tensor_f64_clone(t._ptr))
+    dst = torch.as_tensor(_DeviceSpan(t.device_ptr_mut(), 12), device="cuda")
+    src = torch.arange(12, dtype=torch.float64, device="cuda")
+    dst.copy_(src)
+    torch.cuda.synchronize()
+    got = t.to_numpy()
+    np.testing.assert_array_equal(got, np.arange(12.0).reshape(3, 4).T)  # column-major
+    np.testing.assert_array_equal(keep.to_numpy(), np.zeros((4, 3)))
+    e = gpu.contract(t, (1, -1), gpu.TensorF64.from_numpy(np.ones(3)), (-1,)).to_numpy()
+    np.testing.assert_allclose(e, got.sum(axis=1), rtol=1e-15)
+    bs = gpu.blocksparse
+    b = bs.BlockSparseF64.zeros([[2, 3], [4]], [(1, 0), (0, 0)])
+    view = torch.as_tensor(_DeviceSpan(b.device_ptr_mut(), b.nnz), device="cuda")
+    view.copy_(torch.arange(b.nnz, dtype=torch.float64, device="cuda") + 1)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(b.to_numpy_data(), np.arange(b.nnz) + 1.0)

@@ -1,8 +1,9 @@
 """Sharded block-sparse contraction on 2 GPUs over NCCL.
 
-Each rank computes its FLOP-balanced share of the output blocks
-(contract_shard) and the shards are gathered in HBM (allgather: one NCCL
-broadcast per rank into a single device buffer).  The gathered tensor must
+Each rank computes its cost-balanced share of the output blocks
+(contract_shard, contract_through_diag) and the shards are gathered in HBM
+(allgather: one NCCL all_gather of every rank's blocks, put in sorted order
+by one device concatenation).  The gathered tensor must
 equal the unsharded contraction on one GPU.  Runs as two spawned processes,
 one per GPU; skipped when fewer than two devices are visible.
 """
@@ -58,6 +59,11 @@ def _worker(rank, world, port, q):
         ok = gathered.coords == full.coords and np.allclose(
             gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
         results.append(("cfg5 bond 1024 c128", bool(ok), -1, full.nnzblocks))
+        # the same chain through the diagonal as one launch per rank
+        gathered = bs.allgather(bs.contract_through_diag(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], rank, world))
+        ok = gathered.coords == full.coords and np.allclose(
+            gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
+        results.append(("cfg5 bond 1024 c128 through diag", bool(ok), -1, full.nnzblocks))
         q.put((rank, results, None))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, results, repr(e)))
