@@ -326,10 +326,12 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_contract_diag(const ndt_blocksparse_c64
                                                        const long* labels_s, size_t ndim_s, int* status);
 /* (A . S) . B with S a rank-2 diagonal between A and B (no counterpart in the reference): labels_s
  * = {x, y}, both negative; x labels one axis of A, y one axis of B, and every other label of A and B
- * is positive.  Equals contract(contract_diag(A, S), B): A's and B's free axes in label order.  One
- * grouped launch that scales A's contracted index by S's diagonal as it loads A (no A . S
- * intermediate) when S's blocks are square and each coordinate of A's contracted axis meets one S
- * block; otherwise the two contractions in turn.  rank / nranks as in contract_shard (0, 1: all). */
+ * is positive.  Equals contract(contract_diag(A, S), B): A's and B's free axes in label order.
+ * Sharded (nranks > 1): one grouped launch that applies S's diagonal to the contracted index as it
+ * loads the operands (no A . S intermediate) when S's blocks are square and each coordinate of A's
+ * contracted axis meets one S block; unsharded, or otherwise, the two contractions in turn (one pass
+ * over A costs less than the in-GEMM scaling when a rank does all the work).  rank / nranks as in
+ * contract_shard (0, 1: all). */
 ndt_blocksparse_f64* ndt_blocksparse_f64_contract_through_diag(
     const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a, const ndt_diagblocksparse_f64* s,
     const long* labels_s, size_t ndim_s, const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b, int rank,

@@ -163,8 +163,9 @@ struct ShardPlan {
 // A rank-2 diagonal operand S between A and B, contracted with A's axis
 // `a_axis` on one side and with B on the other: S block (q_a, q_b) maps A's
 // coordinate q_a on that axis to B's coordinate q_b, and its diagonal starts
-// at `off` in S's packed values.  The grouped GEMM scales A's k index by
-// those values as it loads A, so A . S is never formed.
+// at `off` in S's packed values.  The grouped GEMM applies those values to
+// the contracted index as it loads its operands (to B's fragments in shared
+// memory), so A . S is never formed.
 struct ThroughDiag {
   size_t a_axis = 0;
   std::map<size_t, std::pair<size_t, int64_t>> qmap;  // q_a -> (q_b, off)
@@ -689,9 +690,10 @@ BlockSparseT bs_contract_diag(const BlockSparseT& A, const std::vector<int32_t>&
 // with B (one axis); every other label of A and B is positive.  The result is
 // contract(contract_diag(A, la, S, (x, P)), sorted(A's labels) ++ (y), B, lb)
 // for a fresh positive P, i.e. the A-free ++ B-free axes in label order.
-// When S's blocks are square and each of A's coordinates on the contracted
-// axis meets at most one S block, this is ONE grouped launch whose A loads are
-// scaled by S's diagonal (no A . S intermediate); otherwise the two
+// Sharded (nranks > 1), when S's blocks are square and each of A's
+// coordinates on the contracted axis meets at most one S block, this is ONE
+// grouped launch that applies S's diagonal to the contracted index as it
+// loads the operands (no A . S intermediate); otherwise the two
 // contractions run one after the other.  rank / nranks: this rank's share of
 // the output blocks, as contract_shard assigns them.
 BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<int32_t>& la,
@@ -734,6 +736,12 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
     if (t.bsz[0][qa] != t.bsz[1][qb] || td.qmap.count(qa)) fused = false;
     td.qmap[qa] = {qb, (int64_t)t.offs[b]};
   }
+  // Unsharded, one pass over A (HBM bound, 2 |A| bytes) costs less than
+  // applying S inside the GEMM (6-8% of the c128 GEMM); sharded, every rank
+  // would pay that whole pass for its 1/nranks of the work (c128 MPS chain at
+  // bond 8192: unsharded 1.57 ms two-step against 1.64 fused, 8 ranks
+  // 0.23 ms fused against 0.26 two-step).
+  if (nranks == 1) fused = false;
   if (fused) {
     td.sdata = t.nnzb() ? t.st->dev_read() : nullptr;
     td.real = S.real_valued;

@@ -19,8 +19,11 @@
 // dimensions are 16-byte aligned move as 16-byte pairs (VEC).  Shared tiles
 // use padded pitches (4 mod 16 doubles for f64; 2 / 4 mod 8 complex elements
 // for MN- / K-major) so the fragment loads are bank-conflict free.
-// Complex128 uses the 4M real decomposition inside the kernel
-// (Cr += Ar Br - Ai Bi, Ci += Ar Bi + Ai Br) on interleaved (re, im) data.
+// Complex128 uses the 3M real decomposition inside the kernel, on interleaved
+// (re, im) data: three real tensor-core products per complex multiply-add,
+// X += Ar Br, Y += Ai Bi, Z += (Ar + Ai)(Br + Bi), and Cr = X - Y,
+// Ci = Z - X - Y in the epilogue (25% fewer DMMAs than the 4M form; the
+// sums are formed in registers from the staged fragments).
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
@@ -44,7 +47,7 @@ struct KArgs {
   const int4* tiles;  // x = problem, y = tile m index, z = tile n index
   const GroupedProblem* probs;
   const GroupedSegment* segs;
-  const void* kscale;  // grouped mode: per-k scale of A (segments' scale_off), or null
+  const void* kscale;  // grouped mode: per-k scale (segments' scale_off), or null
   int kscale_real;     // complex scale values whose imaginary parts are all zero
   int accumulate;
 };
@@ -115,7 +118,7 @@ struct CopyPlan {
 
 // VEC (f64 only): 16-byte pair copies along the contiguous index; a pair
 // crossing the matrix edge copies 8 bytes and zero-fills the rest.
-// SCALE (grouped only): A(i, k) is multiplied by kscale[scale_off + k] of its
+// SCALE (grouped only): B(k, j) is multiplied by kscale[scale_off + k] of its
 // segment as its fragments leave shared memory, so a diagonal operand between
 // A and B (A . diag(s) . B) costs no pass of its own over A.  1: real scale
 // values (f64, or complex ones with zero imaginary parts: one multiply per
@@ -288,13 +291,15 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
     }
   };
 
-  double acc[MT][NT][4 * RPL];
+  // f64: one accumulator plane; complex (3M): planes X, Y, Z
+  constexpr int PLANES = CPLX ? 3 : 1;
+  double acc[MT][NT][4 * PLANES];
 #pragma unroll
   for (int i = 0; i < MT; i++)
 #pragma unroll
     for (int j = 0; j < NT; j++)
 #pragma unroll
-      for (int q = 0; q < 4 * RPL; q++) acc[i][j][q] = 0.0;
+      for (int q = 0; q < 4 * PLANES; q++) acc[i][j][q] = 0.0;
 
   // ---- prologue
 #pragma unroll
@@ -338,40 +343,6 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
           }
         }
       }
-      if constexpr (SCALE != 0) {
-        // A(i, k) * s(k): fragment column t + 4 (q >> 1) of this k8 step
-        const double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-          const int col = kk + t + 4 * h;
-          if constexpr (CPLX && SCALE == 2) {
-            const double2 sv = *reinterpret_cast<const double2*>(Ss + (size_t)col * 2);
-#pragma unroll
-            for (int i = 0; i < MT; i++)
-#pragma unroll
-              for (int q = 2 * h; q < 2 * h + 2; q++) {
-                const double re = a[i][q], im = ai[i][q];
-                a[i][q] = re * sv.x - im * sv.y;
-                ai[i][q] = re * sv.y + im * sv.x;
-              }
-          } else if constexpr (CPLX) {
-            const double sv = Ss[(size_t)col * 2];
-#pragma unroll
-            for (int i = 0; i < MT; i++)
-#pragma unroll
-              for (int q = 2 * h; q < 2 * h + 2; q++) {
-                a[i][q] *= sv;
-                ai[i][q] *= sv;
-              }
-          } else {
-            const double sv = Ss[col];
-#pragma unroll
-            for (int i = 0; i < MT; i++)
-#pragma unroll
-              for (int q = 2 * h; q < 2 * h + 2; q++) a[i][q] *= sv;
-          }
-        }
-      }
 #pragma unroll
       for (int j = 0; j < NT; j++) {
 #pragma unroll
@@ -388,26 +359,59 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
           }
         }
       }
+      if constexpr (SCALE != 0) {
+        // s(k) B(k, j): fragment row t + 4 q of this k8 step.  B rather than A:
+        // each B fragment belongs to one warp, while the warps of a CTA row
+        // all load the same A fragments, so A would be scaled once per warp.
+        const double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          const int kr = kk + t + 4 * q;
+          if constexpr (CPLX && SCALE == 2) {
+            const double2 sv = *reinterpret_cast<const double2*>(Ss + (size_t)kr * 2);
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+              const double re = b[j][q], im = bi[j][q];
+              b[j][q] = re * sv.x - im * sv.y;
+              bi[j][q] = re * sv.y + im * sv.x;
+            }
+          } else if constexpr (CPLX) {
+            const double sv = Ss[(size_t)kr * 2];
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+              b[j][q] *= sv;
+              bi[j][q] *= sv;
+            }
+          } else {
+            const double sv = Ss[kr];
+#pragma unroll
+            for (int j = 0; j < NT; j++) b[j][q] *= sv;
+          }
+        }
+      }
       if constexpr (!CPLX) {
 #pragma unroll
         for (int i = 0; i < MT; i++)
 #pragma unroll
           for (int j = 0; j < NT; j++) dmma(acc[i][j][0], acc[i][j][1], acc[i][j][2], acc[i][j][3], a[i], b[j]);
       } else {
-        double nai[MT][4];
+        double as[MT][4], bs[NT][2];
 #pragma unroll
         for (int i = 0; i < MT; i++)
 #pragma unroll
-          for (int q = 0; q < 4; q++) nai[i][q] = dneg(ai[i][q]);
+          for (int q = 0; q < 4; q++) as[i][q] = a[i][q] + ai[i][q];
+#pragma unroll
+        for (int j = 0; j < NT; j++)
+#pragma unroll
+          for (int q = 0; q < 2; q++) bs[j][q] = b[j][q] + bi[j][q];
 #pragma unroll
         for (int i = 0; i < MT; i++)
 #pragma unroll
           for (int j = 0; j < NT; j++) {
             double* cc = acc[i][j];
-            dmma(cc[0], cc[1], cc[2], cc[3], a[i], b[j]);
-            dmma(cc[0], cc[1], cc[2], cc[3], nai[i], bi[j]);
-            dmma(cc[RPL * 2], cc[RPL * 2 + 1], cc[RPL * 2 + 2], cc[RPL * 2 + 3], a[i], bi[j]);
-            dmma(cc[RPL * 2], cc[RPL * 2 + 1], cc[RPL * 2 + 2], cc[RPL * 2 + 3], ai[i], b[j]);
+            dmma(cc[0], cc[1], cc[2], cc[3], a[i], b[j]);      // X += Ar Br
+            dmma(cc[4], cc[5], cc[6], cc[7], ai[i], bi[j]);    // Y += Ai Bi
+            dmma(cc[8], cc[9], cc[10], cc[11], as[i], bs[j]);  // Z += (Ar + Ai)(Br + Bi)
           }
       }
     }
@@ -428,7 +432,8 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
         if (row < m && col < n) {
           if constexpr (CPLX) {
             double2* p = reinterpret_cast<double2*>(Cb) + (row + col * ldc);
-            double2 v = make_double2(acc[i][j][q], acc[i][j][4 + q]);
+            const double x = acc[i][j][q], y = acc[i][j][4 + q], z = acc[i][j][8 + q];
+            double2 v = make_double2(x - y, z - x - y);
             if (args.accumulate) {
               double2 o = *p;
               v.x += o.x;
@@ -474,9 +479,16 @@ void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
 // workloads):
 //   f64   0: 64x64x32, 4 warps, two CTAs per SM        1.00
 //         1: 128x128x32, 8 warps, one CTA per SM       0.97
-//   c128  0: 64x64x16, 4 warps, two CTAs per SM        1.00 (35.6 TFLOP/s on 4096 x 4096 x 1024)
-//         1: 64x128x16, 8 warps, one CTA per SM        0.93
-//         2: 32x64x16, 2 warps                         0.85
+//   c128 (3M, 32 x 16 warp tiles: three accumulator planes; 42 TFLOP/s of
+//         complex work, 8mnk, on 2048^3, against 33.5 for the 4M kernel and
+//         36.3 for cuBLAS zgemm)
+//         0: 32x64x16, 4 warps, two CTAs per SM        1.00
+//         1: 64x32x16, 4 warps, two CTAs per SM        0.99
+//         2: 32x32x16, 2 warps, four CTAs per SM       0.90 (0.985 on dense
+//            GEMMs; the lower weight charges its per-tile fill and epilogue,
+//            which short-k block-sparse tiles do not amortise)
+//         (a 64x64 class of 8 warps fits one CTA per SM by registers and ran
+//         10% slower: its barriers stall the whole SM)
 // Smaller tiles waste less on the ragged edges of small blocks and fill the
 // SMs with fewer tiles; the heuristic weighs that against the rate.
 struct TileClass {
@@ -484,7 +496,7 @@ struct TileClass {
   double rate;
 };
 const TileClass kF64Classes[] = {{64, 64, 2, 1.0}, {128, 128, 1, 0.97}};
-const TileClass kC128Classes[] = {{64, 64, 2, 1.0}, {64, 128, 1, 0.93}, {32, 64, 2, 0.85}};
+const TileClass kC128Classes[] = {{32, 64, 2, 1.0}, {64, 32, 2, 0.99}, {32, 32, 4, 0.90}};
 int nclasses(bool cplx) { return cplx ? 3 : 2; }
 const TileClass& tile_class(bool cplx, int cls) { return cplx ? kC128Classes[cls] : kF64Classes[cls]; }
 
@@ -497,11 +509,11 @@ void launch(const KArgs& a, int grid, int cls, cudaStream_t s) {
       launch_cfg<false, 64, 64, 32, 2, 2, 3, AK, BKM, VEC>(a, grid, s);
   } else {
     if (cls == 2)
-      launch_cfg<true, 32, 64, 16, 1, 2, 3, AK, BKM, false>(a, grid, s);
+      launch_cfg<true, 32, 32, 16, 1, 2, 3, AK, BKM, false>(a, grid, s);
     else if (cls == 1)
-      launch_cfg<true, 64, 128, 16, 2, 4, 3, AK, BKM, false>(a, grid, s);
+      launch_cfg<true, 64, 32, 16, 2, 2, 3, AK, BKM, false>(a, grid, s);
     else
-      launch_cfg<true, 64, 64, 16, 2, 2, 3, AK, BKM, false>(a, grid, s);
+      launch_cfg<true, 32, 64, 16, 1, 4, 3, AK, BKM, false>(a, grid, s);
   }
 }
 

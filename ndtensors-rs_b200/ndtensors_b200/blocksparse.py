@@ -503,9 +503,12 @@ def contract_through_diag(a, labels_a, s, labels_s, b, labels_b, rank: int = 0, 
     label is contracted with one axis of A, its second with one axis of B,
     and every other label of A and B is positive.  The result is
     contract(contract_diag(A, S), B): the free axes of A and B in label
-    order.  Runs as one grouped launch that scales A's contracted index by
-    S's diagonal while loading A (no A . S intermediate) when S's blocks are
-    square and each coordinate of A's contracted axis meets one S block.
+    order.  Sharded (nranks > 1), runs as one grouped launch that applies
+    S's diagonal to the contracted index while loading the operands (no
+    A . S intermediate) when S's blocks are square and each coordinate of
+    A's contracted axis meets one S block; unsharded, the two contractions
+    in turn (one pass over A costs less than the in-GEMM scaling when a rank
+    does all the work).
     rank / nranks: this rank's share of the output blocks (contract_shard's
     assignment)."""
     la, na = _labels(labels_a)

@@ -350,21 +350,27 @@ def test_through_diag_cfg5_reduced_bond(gpu, oracle):
     A, S, B = cfg5_tensors(bond=1024)
     bs = gpu.blocksparse
     gA, gS, gB = bs.BlockSparseC64.from_blocks(*A), bs.DiagBlockSparseC64.from_blocks(*S), bs.BlockSparseC64.from_blocks(*B)
-    n0 = gpu.launch_count()
     C = bs.contract_through_diag(gA, [1, 2, -1], gS, [-1, -2], gB, [-2, 3, 4])
-    assert gpu.launch_count() - n0 == 1  # one grouped GEMM, no scaling pass
+    n0 = gpu.launch_count()
+    bs.contract_through_diag(gA, [1, 2, -1], gS, [-1, -2], gB, [-2, 3, 4], 0, 2)
+    assert gpu.launch_count() - n0 == 1  # sharded: one grouped GEMM, no scaling pass
     ref = _through_diag_ref(oracle, A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4])
     assert C.coords == ref.coords and C.block_sizes == ref.block_sizes
     assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
     two = bs.contract(bs.contract_diag(gA, [1, 2, -1], gS, [-1, 5]), [1, 2, -1], gB, [-1, 3, 4])
     assert two.coords == C.coords
     assert rel_fro(C.to_numpy_data(), two.to_numpy_data()) <= RTOL
-    # sharded: every rank's blocks together are the full result, bit for bit
+    # sharded (fused): every rank's blocks together are the full result; the
+    # same kernel arithmetic on every split, bit for bit
+    first = None
     for n in (2, 3, 8):
         shards = [bs.contract_through_diag(gA, [1, 2, -1], gS, [-1, -2], gB, [-2, 3, 4], r, n) for r in range(n)]
         coords, data = merge_shards(shards)
         assert coords == C.coords
-        assert np.array_equal(data, C.to_numpy_data())
+        assert rel_fro(data, ref.data) <= RTOL
+        if first is None:
+            first = data
+        assert np.array_equal(data, first)
 
 
 @pytest.mark.parametrize("cplx", [False, True])
@@ -389,10 +395,15 @@ def test_through_diag_layouts_vs_oracle(gpu, oracle, cplx, la, lb):
     bs = gpu.blocksparse
     cls = _cls(gpu, cplx)
     dcls = bs.DiagBlockSparseC64 if cplx else bs.DiagBlockSparseF64
-    C = bs.contract_through_diag(cls.from_blocks(*A), la, dcls.from_blocks(*S), [-1, -2], cls.from_blocks(*B), lb)
+    gA, gS, gB = cls.from_blocks(*A), dcls.from_blocks(*S), cls.from_blocks(*B)
+    C = bs.contract_through_diag(gA, la, gS, [-1, -2], gB, lb)  # unsharded: two contractions
     ref = _through_diag_ref(oracle, A, la, S, [-1, -2], B, lb)
     assert C.coords == ref.coords and C.block_sizes == ref.block_sizes
     assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
+    # sharded: the fused launch (S applied to the operand loads)
+    coords, data = merge_shards([bs.contract_through_diag(gA, la, gS, [-1, -2], gB, lb, r, 2) for r in range(2)])
+    assert coords == ref.coords
+    assert rel_fro(data, ref.data) <= RTOL
 
 
 def test_through_diag_fallbacks_and_errors(gpu, oracle):
@@ -410,11 +421,13 @@ def test_through_diag_fallbacks_and_errors(gpu, oracle):
                     [(0, 0), (0, 1)]):             # one coordinate, two blocks: two-step
         nd = sum(min(ksz[c[0]], ksz[c[1]]) for c in scoords)
         S = ([ksz, ksz], scoords, rng.standard_normal(nd))
-        C = bs.contract_through_diag(cls.from_blocks(*A), [1, -1], dcls.from_blocks(*S), [-1, -2],
-                                     cls.from_blocks(*B), [-2, 2])
         ref = _through_diag_ref(oracle, A, [1, -1], S, [-1, -2], B, [-2, 2])
-        assert C.coords == ref.coords
-        assert rel_fro(C.to_numpy_data(), ref.data) <= RTOL
+        for n in (1, 2):
+            shards = [bs.contract_through_diag(cls.from_blocks(*A), [1, -1], dcls.from_blocks(*S), [-1, -2],
+                                               cls.from_blocks(*B), [-2, 2], r, n) for r in range(n)]
+            coords, data = merge_shards(shards)
+            assert coords == ref.coords
+            assert rel_fro(data, ref.data) <= RTOL
     S = dcls.from_blocks([ksz, ksz], [(0, 0)], np.ones(3))
     gA, gB = cls.from_blocks(*A), cls.from_blocks(*B)
     for la, ls, lb in (([1, -1], [-1, 2], [-2, 2]),     # S label not negative
