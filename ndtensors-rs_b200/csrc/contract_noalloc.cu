@@ -9,7 +9,9 @@
 // output axes are A's positive labels then B's, unmatched negative labels are
 // pinned at index 0, a scalar result has shape [1]), on caller-owned device
 // buffers.  Operands that have to be packed before the FP64 tensor-core GEMM
-// are packed into the fixed scratch array below instead of pool memory.
+// are packed into the fixed scratch array below instead of pool memory, and
+// the GEMM always runs as one launch (never split along k, which would need a
+// workspace for the partial sums).
 //
 // Scratch: g_noalloc_scratch, kNoAllocScratchBytes (16 MiB) per device, held
 // by every GPU that loads the library until the process exits.  Requests that
@@ -183,7 +185,8 @@ extern "C" int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shap
     double* scr_b = scratch + (size_t)(m * k);
     GemmOperand ga = operand(a, M, KA, m, k, scr_a, s);
     GemmOperand gb = operand(b, N, KB, n, k, scr_b, s);
-    gemm(DType::F64, m, n, k, ga, gb, c, std::max<int64_t>(m, 1), false, s);
+    // No split-K: its partial sums would need a workspace from the pool.
+    gemm(DType::F64, m, n, k, ga, gb, c, std::max<int64_t>(m, 1), false, s, /*allow_split_k=*/false);
     return NDT_SUCCESS;
   } catch (const Error& e) {
     set_last_error(e.what());

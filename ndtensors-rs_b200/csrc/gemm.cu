@@ -547,7 +547,7 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 }  // namespace
 
 void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand B, void* Cp, int64_t ldc,
-          bool accumulate, cudaStream_t s) {
+          bool accumulate, cudaStream_t s, bool allow_split_k) {
   if (m <= 0 || n <= 0) return;
   const bool cplx = dt == DType::C128;
   const DeviceCtx& c = ctx();
@@ -577,7 +577,7 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
     const double slots = (double)c.sm_count * tc.per_sm;
     auto fill = [&](int S) { return tiles * S / (std::ceil(tiles * S / slots) * slots) * (S > 1 ? 0.97 : 1.0); };
     int S = 1;
-    for (int cand = 2; cand <= 4; cand++)
+    for (int cand = 2; cand <= 4 && allow_split_k; cand++)
       if (k / cand >= 16 * 32 && fill(cand) > fill(S) + 0.02) S = cand;
     if (S > 1) {
       std::vector<GroupedProblem> probs(S);

@@ -204,8 +204,10 @@ struct GemmOperand {
   int64_t ld;
   bool kmajor;
 };
+// allow_split_k = false keeps the launch free of device allocations (split-K
+// needs a pool-allocated workspace for its partial sums).
 void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand B, void* C,
-          int64_t ldc, bool accumulate, cudaStream_t s);
+          int64_t ldc, bool accumulate, cudaStream_t s, bool allow_split_k = true);
 
 // Strided views used by the contraction driver: an axis of one operand
 // (extent, element stride) and a contracted axis pair (extent, stride in A,

@@ -6,8 +6,9 @@ operands into a fixed scratch array compiled into the library instead of
 calling cudaMalloc.  This test calls it through the C ABI on caller-owned
 device buffers and compares the result with ndt_tensor_f64_contract on the
 same inputs, on two calls in a row (the scratch array keeps the previous
-call's contents, which must not leak into the next result).  The file name
-makes pytest collect it last.
+call's contents, which must not leak into the next result), and checks through
+the device's default memory pool (the one the library allocates from) that a
+call takes no memory from it.  The file name makes pytest collect it last.
 """
 
 from __future__ import annotations
@@ -27,10 +28,15 @@ def rel_fro(x, y):
     return np.linalg.norm((np.asarray(x) - np.asarray(y)).ravel()) / np.linalg.norm(np.asarray(y).ravel())
 
 
-def _noalloc(lib, torch, a, la, b, lb, out_len):
+def _device_operands(torch, a, b, out_len):
     A = torch.from_numpy(np.asfortranarray(a).ravel(order="F").copy()).cuda()
     B = torch.from_numpy(np.asfortranarray(b).ravel(order="F").copy()).cuda()
     C = torch.full((out_len,), float("nan"), dtype=torch.float64, device="cuda")
+    return A, B, C
+
+
+def _noalloc(lib, torch, a, la, b, lb, out_len, bufs=None):
+    A, B, C = bufs if bufs is not None else _device_operands(torch, a, b, out_len)
     out_shape = (SZ * (a.ndim + b.ndim + 1))()
     out_ndim = SZ(0)
     st = lib.ndt_b200_contract_f64_noalloc(
@@ -50,6 +56,9 @@ CASES = [
     ((16, 4, 32), (1, 2, -1), (32, 4, 16), (-1, 3, 4)),
     # unmatched negative label pinned at index 0, ragged sizes
     ((5, 3, 11), (1, -9, -1), (11, 13), (-1, 2)),
+    # long k over a small output: the regular entry point splits k, this one
+    # runs one launch (scratch bound exactly 16 MiB)
+    ((512, 2048), (1, -1), (2048, 512), (-1, 2)),
 ]
 
 
@@ -78,3 +87,52 @@ def test_noalloc_rejects_oversize_scratch(gpu):
     st, _ = _noalloc(lib, torch, a, [-1, 1], b, [-1, 2], 2000)
     assert st == -1
     assert "scratch" in gpu.last_error()
+
+
+def _pool_used(torch):
+    """(current, high watermark) bytes in use from the device's default memory pool."""
+    from cuda.bindings import runtime as rt
+
+    err, pool = rt.cudaDeviceGetDefaultMemPool(torch.cuda.current_device())
+    assert err == rt.cudaError_t.cudaSuccess, err
+    err, cur = rt.cudaMemPoolGetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    err, high = rt.cudaMemPoolGetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh)
+    assert err == rt.cudaError_t.cudaSuccess, err
+    return int(cur), int(high), pool
+
+
+def _reset_pool_high(torch):
+    from cuda.bindings import driver as dr
+    from cuda.bindings import runtime as rt
+
+    torch.cuda.synchronize()
+    _, _, pool = _pool_used(torch)
+    (err,) = rt.cudaMemPoolSetAttribute(pool, rt.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh, dr.cuuint64_t(0))
+    assert err == rt.cudaError_t.cudaSuccess, err
+    cur, _, _ = _pool_used(torch)
+    return cur
+
+
+def test_noalloc_takes_no_pool_memory(gpu):
+    """The regular entry point takes its output (and split-K workspace) from the
+    pool; the allocation-free one must leave the pool's high watermark where it
+    was, on the long-k shape where the regular GEMM would split k."""
+    import torch
+
+    lib = gpu.get_lib()
+    rng = np.random.default_rng(7)
+    a, b = rng.standard_normal((512, 2048)), rng.standard_normal((2048, 512))
+    ta, tb = gpu.TensorF64.from_numpy(a), gpu.TensorF64.from_numpy(b)
+    before = _reset_pool_high(torch)
+    ref = gpu.contract(ta, [1, -1], tb, [-1, 2])
+    torch.cuda.synchronize()
+    assert _pool_used(torch)[1] > before, "the pool watermark does not see the library's allocations"
+    ref = ref.to_numpy()
+    bufs = _device_operands(torch, a, b, ref.size)
+    for _ in range(2):
+        before = _reset_pool_high(torch)
+        st, got = _noalloc(lib, torch, a, [1, -1], b, [-1, 2], ref.size, bufs)
+        assert st == 0, gpu.last_error()
+        assert _pool_used(torch)[1] <= before
+        assert rel_fro(got, ref) <= RTOL
