@@ -1,7 +1,7 @@
 /*
  * ndt_oracle.c — CPU oracle for the ndtensors contraction hot path.
  *
- * TEST INFRASTRUCTURE ONLY: the checker for tests/, smoke() and bench.py's
+ * TEST INFRASTRUCTURE ONLY: the reference answer for tests/, smoke() and bench.py's
  * CPU-baseline leg.  Never part of the product path.
  *
  * Each function restates one reference algorithm (ndtensors-rs,

@@ -3,7 +3,7 @@
  *
  * TEST INFRASTRUCTURE ONLY.  This is a plain-C restatement of the reference
  * implementation's algorithms (ndtensors-rs, crates/ndtensors/src/...), used as
- * the checker in tests/, in __graft_entry__.smoke() and as the timed CPU
+ * the reference answer in tests/, in __graft_entry__.smoke() and as the timed CPU
  * baseline in bench.py.  The product library (libndtensors_capi.so) never
  * links, loads or calls it.
  *

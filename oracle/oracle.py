@@ -1,7 +1,7 @@
 """ctypes front end of the CPU oracle (oracle/liboracle.so).
 
 TEST INFRASTRUCTURE ONLY: used by tests/, __graft_entry__.smoke() and the CPU
-baseline leg of bench.py as the checker.  The product never imports it.
+baseline leg of bench.py as the reference answer.  The product never imports it.
 
 Arrays are numpy arrays in column-major (Fortran) order, float64 or
 complex128.  Every function returns (status, result) with status one of the

@@ -1,7 +1,7 @@
 """Dense contraction on the GPU (DMMA GEMM + gather) vs the oracle.
 
 Tolerance: relative Frobenius error <= 1e-12 for f64 and complex128 (the
-bound the north-star workload sets); the oracle sums in a different order
+parity bound of this contraction path); the oracle sums in a different order
 (plain i-j-k loop) so bit equality is not expected.
 """
 

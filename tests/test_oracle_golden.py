@@ -2,7 +2,7 @@
 
 Every case of tests/golden/known_answers.json is a test of the reference
 (file:line in the case's `source`).  The oracle must reproduce each asserted
-value and status before it is trusted as the checker of the CUDA path.
+value and status before it is trusted as the reference answer for the CUDA path.
 """
 
 from __future__ import annotations

@@ -16,7 +16,7 @@ from typing import List, Tuple
 
 import numpy as np
 
-# 9 charge sectors q = -4..4 per index
+# U(1) rank-4 block-sparse: 9 charge sectors q = -4..4 per index
 CFG4_SECTORS = list(range(-4, 5))
 CFG4_DIMS_FULL = [8, 24, 56, 96, 144, 96, 56, 24, 8]
 
@@ -51,7 +51,7 @@ def cfg4_tensors(scale: int = 2, seed: int = 1004):
     return (sizes, coords, a), (sizes, coords, b), [1, 2, -1, -2], [-1, -2, 3, 4]
 
 
-# bond 8192 in 33 sectors q = -16..16, Gaussian profile (sigma 6
+# c128 two-site MPS: bond 8192 in 33 sectors q = -16..16, Gaussian profile (sigma 6
 # sectors), largest-remainder rounding to the bond dimension; phys {0, 1}
 CFG5_DIMS_8192 = [16, 24, 36, 52, 74, 102, 137, 178, 225, 278, 332, 387, 439, 484, 518, 540, 548, 540, 518, 484,
                   439, 387, 332, 278, 225, 178, 137, 102, 74, 52, 36, 24, 16]
@@ -122,7 +122,7 @@ def flops_blocksparse(Asp, la, Bsp, lb, complex_: bool) -> float:
     return tot
 
 
-# configs[2]: DMRG environment-update chain, bond D (1024 in the benchmark),
+# DMRG environment-update chain, bond D (1024 in the benchmark),
 # MPO bond 5, physical dimension 2.  Entries N(0,1)/sqrt(fan-in), the fan-in
 # being the product of the axes the tensor contracts in its step.
 CFG3_STEPS = [
