@@ -34,6 +34,16 @@ def set_stream(stream_ptr) -> None:
     check_status(get_lib().ndt_b200_set_stream(ctypes.c_void_p(stream_ptr) if stream_ptr else None), "set_stream")
 
 
+def __getattr__(name: str):
+    """``torch_contract`` loads on first use, as in the reference binding
+    (python/ndtensors_rs/src/ndtensors_rs/__init__.py)."""
+    if name == "torch_contract":
+        from .torch_ops import torch_contract
+
+        return torch_contract
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")
+
+
 __all__ = [
     "TensorF64",
     "TensorC64",

@@ -108,9 +108,13 @@ class _DenseBase:
         if not t.is_cuda:
             return cls.from_numpy(t.numpy())
         want = torch.complex128 if cls._width == 2 else torch.float64
-        tt = t.to(want).permute(*reversed(range(t.dim()))).contiguous()
+        tt = t.to(want).permute(tuple(reversed(range(t.dim())))).contiguous()
         shape = tuple(t.shape)
         n = max(1, tt.numel())
+        if tt.numel() == 0:
+            tt = torch.zeros(1, dtype=want, device=t.device)  # storage holds max(1, prod) elements
+        # torch wrote tt on its own stream; the library copies it on another
+        torch.cuda.current_stream(tt.device).synchronize()
         status = ctypes.c_int(-999)
         ptr = getattr(get_lib(), f"ndt_tensor_{cls._prefix}_from_device_ptr")(
             ctypes.c_void_p(tt.data_ptr()), n, _shape_arr(shape), len(shape), ctypes.byref(status)

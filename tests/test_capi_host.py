@@ -195,3 +195,17 @@ def test_compute_without_device_fails_loudly(ndt):
     assert "no CUDA device" in ndt.last_error()
     with pytest.raises(ndt.NDTensorsError):
         ndt.contract(ndt.TensorF64.ones((2, 3)), (1, -1), ndt.TensorF64.ones((3, 4)), (-1, 2))
+
+
+@pytest.mark.skipif("__import__('ndtensors_b200').device_available()", reason="a CUDA device is present")
+def test_torch_contract_has_no_cpu_path(ndt):
+    """torch_contract resolves lazily from the package, as the reference
+    binding's does, and without a device it raises instead of computing."""
+    import torch
+
+    from ndtensors_b200.torch_ops import TORCH_AVAILABLE
+
+    assert TORCH_AVAILABLE
+    tc = ndt.torch_contract
+    with pytest.raises(ndt.NDTensorsError):
+        tc(torch.ones((2, 3)), (1, -1), torch.ones((3, 4)), (-1, 2))
