@@ -130,3 +130,66 @@ def test_allgather_shards_gloo(world, cplx, interleaved):
     for p in ps:
         p.join(timeout=60)
     assert sorted(res) == [(r, True) for r in range(world)]
+
+
+def _gather_failure_worker(rank, world, port, q, mode):
+    """Rank 1 fails before the gather: it exits ("exit") or stays alive but
+    never joins the collective ("absent"); rank 0 must get an error from
+    allgather within the process group's timeout, not hang."""
+    import sys
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+    import datetime
+
+    import torch.distributed as dist
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "ndtensors-rs_b200"))
+    import ndtensors_b200 as ndt
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    shard = ndt.blocksparse.BlockSparseF64.from_blocks([[2, 3], [4]], [(rank, 0)], np.ones(8 if rank == 0 else 12))
+    if rank == 1:
+        if mode == "exit":
+            os._exit(3)  # the process dies without a word to its peers
+        time.sleep(8)  # alive past the 5 s timeout, but never reaches the gather
+        q.put((rank, "absent"))
+        q.close()
+        q.join_thread()  # flush before the hard exit
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        ndt.blocksparse.allgather(shard)
+        q.put((rank, "no error", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001 - any error ends the wait, which is what is checked
+        q.put((rank, type(e).__name__, time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)  # skip process-group teardown with a lost peer
+
+
+@pytest.mark.parametrize("mode", ["exit", "absent"])
+def test_allgather_fails_when_a_rank_is_lost(mode):
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ps = [ctx.Process(target=_gather_failure_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(2 if mode == "absent" else 1):
+        r = q.get(timeout=60)
+        res[r[0]] = r[1:]
+    for p in ps:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    outcome, waited = res[0]
+    assert outcome != "no error"
+    assert waited < 30  # bounded by the 5 s process-group timeout, not a hang
