@@ -582,9 +582,11 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
     if (S > 1) {
       std::vector<GroupedProblem> probs(S);
       std::vector<GroupedSegment> segs(S);
-      const int64_t kc = (k / S + 31) / 32 * 32;
+      // Pieces of ceil(k / S) rounded up to 32, the last one ending at k: the
+      // pieces cover k exactly (k / S >= 512 keeps every piece non-empty).
+      const int64_t kc = ((k + S - 1) / S + 31) / 32 * 32;
       for (int sp = 0; sp < S; sp++) {
-        const int64_t k0 = sp * kc, k1 = std::min<int64_t>(k, k0 + kc);
+        const int64_t k0 = sp * kc, k1 = (sp == S - 1) ? k : std::min<int64_t>(k, k0 + kc);
         probs[sp] = GroupedProblem{m, n, (int64_t)sp * m * n, sp, 1};
         segs[sp] = GroupedSegment{A.kmajor ? k0 : k0 * A.ld, B.kmajor ? k0 : k0 * B.ld, k1 - k0, A.ld, B.ld, -1};
       }

@@ -101,6 +101,27 @@ def test_contract_zero_extent_is_internal_error(gpu):
     assert st.value == -4
 
 
+@pytest.mark.parametrize("m,n,k", [(1024, 512, 1025), (768, 512, 1537), (512, 512, 2049), (512, 512, 2048),
+                                   (512, 512, 4095)])
+def test_split_k_pieces_cover_k(gpu, m, n, k):
+    """Grids with a mostly idle last wave and a long k run split-K (2, 3 and 4
+    pieces for these shapes); k not a multiple of the piece count times 32
+    must still be covered to its last index."""
+    rng = np.random.default_rng(m + n + k)
+    a, b = rng.standard_normal((m, k)), rng.standard_normal((k, n))
+    got = gpu.contract(gpu.TensorF64.from_numpy(a), (1, -1), gpu.TensorF64.from_numpy(b), (-1, 2)).to_numpy()
+    assert rel_fro(got, a @ b) <= RTOL
+
+
+def test_split_k_pieces_cover_k_c128(gpu):
+    """complex128 (3M kernel) through split-K: 512 x 512 x 1025 runs 2 pieces."""
+    rng = np.random.default_rng(1025)
+    a = rng.standard_normal((512, 1025)) + 1j * rng.standard_normal((512, 1025))
+    b = rng.standard_normal((1025, 512)) + 1j * rng.standard_normal((1025, 512))
+    got = gpu.contract(gpu.TensorC64.from_numpy(a), (1, -1), gpu.TensorC64.from_numpy(b), (-1, 2)).to_numpy()
+    assert rel_fro(got, a @ b) <= RTOL
+
+
 def test_mps_merge_full_size(gpu, oracle):
     """Dense f64 MPS two-site merge at full size: A[256,4,256] x B[256,4,256]
     contracting A's last with B's first -> C[256,4,4,256]; N(0,1) seed 1001."""
