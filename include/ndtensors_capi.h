@@ -136,11 +136,16 @@ ndt_tensor_c64* ndt_tensor_c64_contract_gemm(const ndt_tensor_c64* a, const long
 
 /* Device-pointer interop (the device-pointer ABI proposed in the reference's
  * README, "CUDA support" section).  from_device_ptr copies `len` elements from
- * device memory of the current device; device_ptr returns the tensor's device
- * buffer for reading (valid until mutation / release; work on it is ordered on
- * the library stream); device_ptr_mut returns it for writing from outside the
- * library (copy on write if shared, as data_mut; the device copy then holds
- * the tensor's values, and host views are refreshed from it). */
+ * device memory of the current device (the caller's writes to it must be
+ * complete) and returns once they have been read; device_ptr returns the
+ * tensor's device buffer for reading (valid until mutation / release);
+ * device_ptr_mut returns it for writing from outside the library (copy on
+ * write if shared, as data_mut; the device copy then holds the tensor's
+ * values, and host views are refreshed from it).  Both return once the
+ * library's pending work on the buffer (fills, uploads, kernels) has
+ * completed, so reads and writes from any stream are safe.  With a caller
+ * stream installed by ndt_b200_set_stream all three return at once, the work
+ * being ordered on that stream. */
 ndt_tensor_f64* ndt_tensor_f64_from_device_ptr(const double* dptr, size_t len, const size_t* shape, size_t ndim,
                                                int* status);
 const double* ndt_tensor_f64_device_ptr(const ndt_tensor_f64* tensor);

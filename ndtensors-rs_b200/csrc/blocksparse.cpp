@@ -1033,7 +1033,10 @@ extern "C" {
   const double* ndt_blocksparse_##DT##_device_ptr(const T* t) {                                                      \
     if (!t) return nullptr;                                                                                          \
     try {                                                                                                            \
-      return (const double*)((const NdtBs*)t)->t.st->dev_read();                                                     \
+      Storage& st = *((const NdtBs*)t)->t.st;                                                                        \
+      const double* p = (const double*)st.dev_read();                                                                \
+      settle_for_caller(st.device);                                                                                  \
+      return p;                                                                                                      \
     } catch (const std::exception& e) {                                                                              \
       set_last_error(e.what());                                                                                      \
       return nullptr;                                                                                                \
@@ -1044,7 +1047,9 @@ extern "C" {
     try {                                                                                                            \
       BlockSparseT& b = ((NdtBs*)t)->t;                                                                              \
       if (b.st.use_count() > 1) b.st = b.st->clone(); /* copy on write */                                            \
-      return (double*)b.st->dev_write();                                                                             \
+      double* p = (double*)b.st->dev_write();                                                                        \
+      settle_for_caller(b.st->device);                                                                               \
+      return p;                                                                                                      \
     } catch (const std::exception& e) {                                                                              \
       set_last_error(e.what());                                                                                      \
       return nullptr;                                                                                                \

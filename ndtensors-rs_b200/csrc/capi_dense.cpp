@@ -306,7 +306,10 @@ void* contract_impl(const void* a, const long* la, size_t na, const void* b, con
 const double* device_ptr_impl(const void* t) {
   if (!t) return nullptr;
   try {
-    return (const double*)H(t)->t.st->dev_read();
+    Storage& st = *H(t)->t.st;
+    const double* p = (const double*)st.dev_read();
+    settle_for_caller(st.device);
+    return p;
   } catch (const std::exception& e) {
     set_last_error(e.what());
     return nullptr;
@@ -318,7 +321,9 @@ double* device_ptr_mut_impl(void* t) {
   try {
     Dense& d = H(t)->t;
     d.make_unique();  // copy on write, as data_mut
-    return (double*)d.st->dev_write();
+    double* p = (double*)d.st->dev_write();
+    settle_for_caller(d.st->device);
+    return p;
   } catch (const std::exception& e) {
     set_last_error(e.what());
     return nullptr;

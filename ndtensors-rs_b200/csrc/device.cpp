@@ -77,6 +77,11 @@ DeviceCtx& ctx(int device) {
 
 DeviceCtx& ctx() { return ctx(current_device()); }
 
+void settle_for_caller(int device) {
+  DeviceCtx& c = ctx(device);
+  if (!c.external_stream) NDT_CUDA(cudaStreamSynchronize(c.compute));
+}
+
 void* dev_alloc(size_t bytes, int device) {
   DeviceCtx& c = ctx(device);
   void* p = nullptr;

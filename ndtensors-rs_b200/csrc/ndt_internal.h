@@ -85,6 +85,14 @@ struct DeviceCtx {
 };
 DeviceCtx& ctx(int device);
 DeviceCtx& ctx();  // current device
+// A tensor's device buffer is being handed to a caller (device_ptr /
+// device_ptr_mut), or a caller's buffer has just been copied in
+// (from_device_ptr).  On the library's own stream, wait for it, so that the
+// caller's reads and writes, on any stream, see the tensor's values, are not
+// overtaken by a fill, upload or kernel still pending for that buffer, and a
+// source buffer may be reused at once.  A caller stream installed with
+// ndt_b200_set_stream already orders them.
+void settle_for_caller(int device);
 // Device memory: stream-ordered allocations from the device's default pool
 // (release threshold raised so freed blocks are reused, not returned).
 void* dev_alloc(size_t bytes, int device);

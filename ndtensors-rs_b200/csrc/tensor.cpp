@@ -216,6 +216,9 @@ Dense make_from_device(DType dt, const void* dptr, size_t len, const std::vector
   if (t.st->len != len) throw Error(ErrKind::ShapeMismatch, "length does not match shape");
   DeviceCtx& c = ctx(t.st->device);
   NDT_CUDA(cudaMemcpyAsync(t.st->dev, dptr, t.st->bytes(), cudaMemcpyDeviceToDevice, c.compute));
+  // Return once the caller's buffer has been read (as from_data does), so it
+  // may be reused or freed from any stream.
+  settle_for_caller(t.st->device);
   return t;
 }
 

@@ -83,11 +83,17 @@ class _BsBase:
 
         want = torch.complex128 if cls._width == 2 else torch.float64
         d = data.to(want).contiguous()
+        if not d.is_cuda:
+            return cls.from_blocks(block_sizes, coords, d.numpy())
         ndim, nblk, bsz, nnzb, cs = _structure_args(block_sizes, coords)
+        # torch wrote d on its own stream; the library copies it on another
+        torch.cuda.current_stream(d.device).synchronize()
         st = ctypes.c_int(-999)
         p = getattr(get_lib(), f"ndt_blocksparse_{cls._prefix}_from_device_ptr")(
             ndim, nblk, bsz, nnzb, cs, ctypes.c_void_p(d.data_ptr()), d.numel(), ctypes.byref(st))
         _raise(st.value, "blocksparse from_device_ptr")
+        # the copy has read d before d (a temporary) goes back to torch
+        check_status(get_lib().ndt_b200_synchronize(), "synchronize")
         return cls(p)
 
     @classmethod
