@@ -102,3 +102,23 @@ def test_contract_operand_past_2pow31_elements(gpu):
     err = float(torch.linalg.norm((got_t - ref_t).flatten()) / torch.linalg.norm(ref_t.flatten()))
     assert err <= RTOL
 
+
+
+def test_blocksparse_block_offset_past_2pow31(gpu):
+    """A's first block holds 46341^2 > 2^31 elements, so the block that the
+    only matched pair reads starts past 2^31 in A's packed data.  The blocks
+    are written through the library (insert_block)."""
+    bs = gpu.blocksparse
+    big = 46341
+    assert big * big > TWO31
+    A = bs.BlockSparseF64.zeros([[big, 8], [big, 8]], [(0, 0), (1, 1)])
+    B = bs.BlockSparseF64.zeros([[big, 8], [4]], [(1, 0)])
+    rng = np.random.default_rng(5)
+    a11, b10 = rng.standard_normal((8, 8)), rng.standard_normal((8, 4))
+    A.insert_block((1, 1), a11)
+    B.insert_block((1, 0), b10)
+    C = bs.contract(A, [1, -1], B, [-1, 2])
+    assert C.coords == [(1, 0)]
+    got = C.to_numpy_data().reshape((8, 4), order="F")
+    ref = a11 @ b10
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) <= RTOL
