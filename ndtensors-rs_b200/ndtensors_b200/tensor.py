@@ -106,7 +106,7 @@ class _DenseBase:
         import torch
 
         if not t.is_cuda:
-            return cls.from_numpy(t.numpy())
+            return cls.from_numpy(t.detach().numpy())
         want = torch.complex128 if cls._width == 2 else torch.float64
         tt = t.to(want).permute(tuple(reversed(range(t.dim())))).contiguous()
         shape = tuple(t.shape)

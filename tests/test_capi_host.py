@@ -209,3 +209,14 @@ def test_torch_contract_has_no_cpu_path(ndt):
     tc = ndt.torch_contract
     with pytest.raises(ndt.NDTensorsError):
         tc(torch.ones((2, 3)), (1, -1), torch.ones((3, 4)), (-1, 2))
+
+
+def test_from_torch_cpu_tensor_with_grad(ndt):
+    """A CPU tensor that requires grad enters the library like any other
+    (host bookkeeping; no device needed)."""
+    import torch
+
+    x = torch.arange(6, dtype=torch.float64).reshape(2, 3).requires_grad_()
+    t = ndt.TensorF64.from_torch(x)
+    assert t.shape == (2, 3)
+    np.testing.assert_array_equal(t.to_numpy(), x.detach().numpy())
