@@ -37,6 +37,8 @@ import threading
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "ndtensors-rs_b200"))
 sys.path.insert(0, str(ROOT))
@@ -410,6 +412,39 @@ def run_reference(args, world, rank):
 
 
 # ------------------------------------------------------------------- ours
+def _r3(x):
+    return None if x is None else float(f"{x:.3g}")
+
+
+def summary_rows(line_head, extras):
+    """One short row per configuration, printed as the line's last key so that
+    a reader of the line's tail sees every configuration's number:
+    [cfg, value, unit, roofline fraction (executed for 3M complex), ms, n_gpus,
+    parity (max relative error checked in this run, or null)]."""
+    rows = [["c2 permute f64 (headline)", _r3(line_head["value"]), "GB/s", _r3(line_head["achieved"] /
+             line_head["peak"]), _r3(line_head["ms"]), line_head["world"], 0.0]]
+    if line_head.get("e2e"):
+        rows.append(["c2 permute f64 e2e (C ABI, host buffers)", _r3(line_head["e2e"]["value"]), "GB/s", None,
+                     None, line_head["world"], None])
+    for e in extras:
+        if "cfg" not in e:
+            continue
+        rf = e.get("roofline") or {}
+        frac = rf.get("executed_frac", rf.get("frac"))
+        par = e.get("parity")
+        perr = None
+        if isinstance(par, dict):
+            perr = _r3(par.get("max_block_rel_err", par.get("rel_err")))
+            if not par.get("ok", False):
+                perr = "FAIL"
+        unit = {"TFLOP/s": "TF/s", "GB/s": "GB/s"}.get(e.get("unit"), e.get("unit"))
+        rows.append([e["cfg"], _r3(e.get("value")), unit, _r3(frac), _r3(e.get("ms")), e.get("n_gpus", 1), perr])
+        if e.get("e2e"):
+            rows.append([e["cfg"] + " e2e", _r3(e["e2e"]["value"]), unit, None, _r3(e["e2e"].get("ms")),
+                         e.get("n_gpus", 1), None])
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -542,7 +577,7 @@ def main():
     b1.record()
     torch.cuda.synchronize()
     batched_gbs = BYTES_F64 * B * args.steps / (b0.elapsed_time(b1) * 1e-3) / 1e9
-    batched_line = {"workload": f"permutedims 16^6 f64 perm (5,3,1,0,4,2), batch of {B} as one rank-7 launch",
+    batched_line = {"cfg": "c2 permute f64 x32 1 launch", "workload": f"permutedims 16^6 f64 perm (5,3,1,0,4,2), batch of {B} as one rank-7 launch",
                     "value": batched_gbs, "unit": "GB/s",
                     "roofline": {"bound": "hbm", "achieved": batched_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                                  "frac": batched_gbs / peaks["hbm_gbs"]}}
@@ -636,6 +671,28 @@ def main():
         extras += run_dmrg(args, torch, ndt, peaks, world, rank, pg)
         extras += run_blocksparse(args, torch, ndt, world, rank, pg)
 
+    if world == 1 and not args.no_extras:
+        e2e_c = contraction_e2e(torch, ndt, lib)
+        for e in extras:
+            if e.get("cfg") in e2e_c and e.get("n_gpus", 1) == 1:
+                e["e2e"] = e2e_c[e["cfg"]]
+
+    # ---- parity of every checked configuration, max over ranks (each rank
+    # checked its own output blocks / slab against the CPU reference)
+    parity_ok = True
+    for e in extras:
+        par = e.get("parity")
+        if not isinstance(par, dict):
+            continue
+        key = "max_block_rel_err" if "max_block_rel_err" in par else "rel_err"
+        t = torch.tensor([float(par.get(key, 0.0)), 0.0 if par.get("ok", False) else 1.0], device="cuda")
+        if pg:
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        par[key] = float(t[0].item())
+        par["ok"] = bool(t[1].item() == 0.0)
+        par["over_ranks"] = world
+        parity_ok = parity_ok and par["ok"]
+
     # ---- CPU baseline (rank 0, N=1 only): the oracle port on one host thread
     if rank == 0 and world == 1 and not args.no_extras:
         cb = cpu_contraction_baselines()
@@ -671,6 +728,10 @@ def main():
                        "l2": f"inputs larger than L2: {B} distinct 134 MB tensors per step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic("permute_16p6_f64"),
+                         "traffic_read": ncu_traffic("permute_16p6_f64_read"),
+                         "traffic_note": "ncu dram bytes inside the launch; part of the 134.2 MB of writes drains "
+                                         "from L2 after the kernel ends and is not counted, so compare traffic_read "
+                                         "with the 134.2 MB of algorithmic reads",
                          "kernel": "permute_tiled_kernel<8>", "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_src})",
                          "algorithmic_bytes_per_launch": BYTES_F64},
             "cpu_baseline": cpu,
@@ -679,11 +740,81 @@ def main():
             "clocks": sampler.result(),
             "host": host_info(),
             "contraction": extras,
+            "summary": summary_rows(line_head={"value": value, "achieved": achieved, "peak": peaks["hbm_gbs"],
+                                               "ms": ms_max / args.steps, "world": world, "e2e": e2e},
+                                    extras=extras),
         }
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+    if not parity_ok:
+        # a rate whose result differs from the reference is not a result
+        raise SystemExit("parity check failed: see the 'parity' keys of the line")
+
+
+def _host_threads(torch, world):
+    """Share the host cores between the ranks of this node for CPU checks."""
+    torch.set_num_threads(max(1, (os.cpu_count() or 8) // max(1, world)))
+
+
+def _device_blocks(torch, bs, t, coords):
+    """{coords: numpy block} of a library block-sparse tensor, copying only
+    the listed blocks from the device."""
+    _, allc, offs = t._structure()
+    allc = [tuple(int(x) for x in c) for c in allc]
+    ends = list(offs[1:]) + [t.nnz]
+    where = {c: (int(o), int(e)) for c, o, e in zip(allc, offs, ends)}
+    cplx = isinstance(t, bs.BlockSparseC64)
+    span = torch.as_tensor(bs._DeviceSpan(t.device_ptr(), t.nnz * (2 if cplx else 1)), device="cuda")
+    out = {}
+    for c in coords:
+        o, e = where[tuple(c)]
+        v = span[(2 if cplx else 1) * o:(2 if cplx else 1) * e].cpu().numpy()
+        out[tuple(c)] = v.view(np.complex128) if cplx else v
+    return out
+
+
+def block_parity(torch, bs, result, A, B, nfree_a, nc, world, kscale=None, cplx=False, every=10,
+                 flop_budget=None, expect_coords=None):
+    """Check a seeded sample of `result`'s output blocks (every `every`-th in
+    sorted order, plus the one with the most flops, within `flop_budget`)
+    against the CPU block reference (tests/blockref.py: per output block, the
+    sum of its pair GEMMs in float64 / complex128, as
+    contract/blocksparse.rs:144-180 computes it).  With `expect_coords`, the
+    result's block list must equal it exactly.  Returns the parity record."""
+    import blockref
+
+    coords = [tuple(int(x) for x in c) for c in result.coords]
+    rec = {"tol": 1e-12, "blocks": len(coords)}
+    if expect_coords is not None:
+        rec["structure_ok"] = coords == [tuple(c) for c in expect_coords]
+    fl = blockref.pair_flops(A, B, nfree_a, nc, coords, cplx)
+    pick = list(coords[::every])
+    if coords:
+        big = max(coords, key=lambda c: fl[c])
+        if big not in pick:
+            pick.append(big)
+    if flop_budget is not None:
+        pick.sort(key=lambda c: fl[c])
+        chosen, used = [], 0.0
+        for c in pick:
+            if used + fl[c] <= flop_budget:
+                chosen.append(c)
+                used += fl[c]
+        pick = chosen
+    _host_threads(torch, world)
+    ref = blockref.reference_blocks(A, B, nfree_a, nc, pick, kscale=kscale)
+    got = _device_blocks(torch, bs, result, pick)
+    errs = [blockref.rel_fro(got[c], ref[c]) for c in pick]
+    num = sum(float(np.linalg.norm(got[c] - ref[c]) ** 2) for c in pick)
+    den = sum(float(np.linalg.norm(ref[c]) ** 2) for c in pick)
+    rec.update({"checked": len(pick), "checked_flop_frac": (sum(fl[c] for c in pick) / max(sum(fl.values()), 1.0)),
+                "max_block_rel_err": max(errs) if errs else 0.0,
+                "rel_err": (num / den) ** 0.5 if den > 0 else 0.0})
+    rec["ok"] = bool(rec["max_block_rel_err"] <= 1e-12 and rec.get("structure_ok", True) and
+                     (len(pick) > 0 or not coords))
+    return rec
 
 
 def run_blocksparse(args, torch, ndt, world, rank, pg):
@@ -724,24 +855,27 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     dB = torch.randn(total, dtype=torch.float64, device="cuda", generator=g)
     A = bs.BlockSparseF64.from_torch(sizes, coords, dA)
     B = bs.BlockSparseF64.from_torch(sizes, coords, dB)
-    del dA, dB
     la, lb = [1, 2, -1, -2], [-1, -2, 3, 4]
     flops = W.flops_blocksparse((sizes, coords, None), la, (sizes, coords, None), lb, False)
     if world == 1:
-        ms, _ = timed(lambda: bs.contract(A, la, B, lb), 3)
+        ms, r = timed(lambda: bs.contract(A, la, B, lb), 3)
     else:
-        ms, _ = timed(lambda: bs.contract_shard(A, la, B, lb, rank, world), 3)
+        ms, r = timed(lambda: bs.contract_shard(A, la, B, lb, rank, world), 3)
+    # the timed result checked against the CPU block reference (the operands
+    # stay on the device; only the blocks a sampled pair uses are copied)
+    par = block_parity(torch, bs, r, (sizes, coords, dA), (sizes, coords, dB), 2, 2, world)
     tf = flops / (ms * 1e-3) / 1e12
-    out.append({"workload": "block-sparse U(1) rank-4 x rank-4 f64, sector dims halved [4,12,28,48,72,48,28,12,4] "
-                            "(489 blocks, 4.25 GB per operand)",
-                "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": flops, "n_gpus": world,
-                "scaling": "strong" if world > 1 else None,
-                "roofline": fp64_roofline(tf / world)})
-    del A, B
+    out.append({"cfg": "c4 U1 half", "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": flops, "n_gpus": world,
+                "scaling": "strong" if world > 1 else None, "parity": par,
+                "roofline": fp64_roofline(tf / world),
+                "workload": "block-sparse U(1) rank-4 x rank-4 f64, sector dims halved [4,12,28,48,72,48,28,12,4] "
+                            "(489 blocks, 4.25 GB per operand)"})
+    del A, B, r, dA, dB
     torch.cuda.empty_cache()
 
     # ---- c128 two-site MPS (A . S) . B, bond 8192, 33 sectors
-    (sa, ca, a), (ss, cs_, sd), (sb, cb, b) = W.cfg5_tensors()
+    Ah, Sh, Bh = W.cfg5_tensors()
+    (sa, ca, a), (ss, cs_, sd), (sb, cb, b) = Ah, Sh, Bh
     A = bs.BlockSparseC64.from_blocks(sa, ca, a)
     S = bs.DiagBlockSparseC64.from_blocks(ss, cs_, sd)
     B = bs.BlockSparseC64.from_blocks(sb, cb, b)
@@ -751,18 +885,29 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
         # one grouped launch per rank: S's diagonal scales A's loads (no A.S pass)
         return bs.contract_through_diag(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], rank, world)
 
-    ms5, _ = timed(chain, 10)
+    ms5, r5 = timed(chain, 10)
+    import blockref
+
+    all5 = blockref.output_coords(Ah, Bh, 2, 1)
+    par5 = block_parity(torch, bs, r5, Ah, Bh, 2, 1, world, kscale=np.asarray(sd), cplx=True, every=1,
+                        expect_coords=all5 if world == 1 else None)
     tf5 = flops5 / (ms5 * 1e-3) / 1e12
-    entry = {"workload": "block-sparse c128 two-site MPS (A.S).B, bond 8192 in 33 sectors, DiagBlockSparse S",
-             "value": tf5, "unit": "TFLOP/s", "ms": ms5, "flop": flops5, "n_gpus": world,
-             "scaling": "strong" if world > 1 else None, "gather": "none (compute only)",
-             "roofline": fp64_roofline(tf5 / world, complex_3m=True)}
+    entry = {"cfg": "c5 c128 MPS", "value": tf5, "unit": "TFLOP/s", "ms": ms5, "flop": flops5, "n_gpus": world,
+             "scaling": "strong" if world > 1 else None, "gather": "none (compute only)", "parity": par5,
+             "roofline": fp64_roofline(tf5 / world, complex_3m=True),
+             "workload": "block-sparse c128 two-site MPS (A.S).B, bond 8192 in 33 sectors, DiagBlockSparse S"}
     out.append(entry)
+    del r5
     if world > 1:
-        msg, _ = timed(lambda: bs.allgather(chain()), 5)
-        out.append({"workload": "block-sparse c128 two-site MPS, sharded + NCCL allgather of the output",
-                    "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": msg, "n_gpus": world,
-                    "scaling": "strong", "gather": "allgather (NCCL) of all output blocks to every rank"})
+        msg, rg = timed(lambda: bs.allgather(chain()), 5)
+        # the gathered tensor: the unsharded block list, every block checked
+        parg = block_parity(torch, bs, rg, Ah, Bh, 2, 1, world, kscale=np.asarray(sd), cplx=True, every=1,
+                            expect_coords=all5)
+        out.append({"cfg": "c5 c128 MPS+gather", "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s",
+                    "ms": msg, "n_gpus": world, "scaling": "strong", "parity": parg,
+                    "gather": "allgather (NCCL) of all output blocks to every rank",
+                    "workload": "block-sparse c128 two-site MPS, sharded + NCCL allgather of the output"})
+        del rg
     if world >= 4:
         del A, S, B
         torch.cuda.empty_cache()
@@ -835,14 +980,20 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
                 g = torch.Generator(device="cuda").manual_seed(seed * 1000 + i)
                 view[off:off + elems[c]].normal_(generator=g)
                 off += elems[c]
-        return t
+        return t, [c for _, c in kept]
 
-    A = make(used_a, 1)
-    B = make(used_b, 2)
+    A, ka = make(used_a, 1)
+    B, kb = make(used_b, 2)
     torch.cuda.synchronize()
-    ms, _ = timed(lambda: bs.contract_select(A, la, B, lb, mine), 1, warm=1)
+    ms, r = timed(lambda: bs.contract_select(A, la, B, lb, mine), 1, warm=1)
     tf = total / (ms * 1e-3) / 1e12
-    return {"workload": "block-sparse U(1) rank-4 x rank-4 f64 at the literal size [8,24,56,96,144,96,56,24,8] "
+    # a sample of this rank's output blocks against the CPU block reference,
+    # within 3e11 flop of host work per rank (the largest blocks are 1e13)
+    span = lambda t: torch.as_tensor(bs._DeviceSpan(t.device_ptr(), t.nnz), device="cuda")  # noqa: E731
+    par = block_parity(torch, bs, r, (sizes, ka, span(A)), (sizes, kb, span(B)), 2, 2, world, flop_budget=3e11,
+                       expect_coords=mine)
+    return {"cfg": "c4 U1 literal", "parity": par,
+            "workload": "block-sparse U(1) rank-4 x rank-4 f64 at the literal size [8,24,56,96,144,96,56,24,8] "
                         "(489 blocks, 68 GB per operand, 6.39e14 flop), each rank holding only the blocks its "
                         "output blocks reference",
             "value": tf, "unit": "TFLOP/s", "ms": ms, "flop": total, "n_gpus": world, "scaling": "strong",
@@ -850,6 +1001,90 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
             "assignment": "longest-processing-time" if use_lpt else "contiguous FLOP-balanced ranges",
             "max_rank_flop_share": max(sum(work[o] for o in lst) for lst in plan) / total,
             "max_rank_gb": max(footprint(lst) for lst in plan) / 1e9}
+
+
+def contraction_e2e(torch, ndt, lib):
+    """End-to-end times of contraction configurations through the C ABI with
+    host buffers (pinned), one host thread, wall clock: every step uploads
+    the inputs (from_data), contracts, and reads the result back (data()).
+    Returns {cfg: {"value": TFLOP/s, "ms", "h2d_bytes_per_step",
+    "d2h_bytes_per_step", "path"}}."""
+    sys.path.insert(0, str(ROOT / "tests"))
+    import workloads as W
+
+    def pinned(x):
+        t = torch.empty(x.size, dtype=torch.float64 if x.dtype == np.float64 else torch.complex128, pin_memory=True)
+        t.numpy()[:] = np.asarray(x).ravel(order="F")
+        return t
+
+    def wall(fn, reps, warm=2):
+        for _ in range(warm):
+            fn()
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        for _ in range(reps):
+            fn()
+        return (time.perf_counter() - w0) / reps * 1e3
+
+    res = {}
+    st = ctypes.c_int(-999)
+    dp = ctypes.POINTER(ctypes.c_double)
+    # ---- c1: MPS merge A[256,4,256] x B[256,4,256] through ndt_tensor_f64_contract
+    rng = np.random.default_rng(1001)
+    a, b = rng.standard_normal((256, 4, 256)), rng.standard_normal((256, 4, 256))
+    pa, pb = pinned(a), pinned(b)
+    shp = (ctypes.c_size_t * 3)(256, 4, 256)
+    la, lb = (ctypes.c_long * 3)(1, 2, -1), (ctypes.c_long * 3)(-1, 3, 4)
+
+    def c1():
+        ta = lib.ndt_tensor_f64_from_data(ctypes.cast(pa.data_ptr(), dp), pa.numel(), shp, 3, ctypes.byref(st))
+        tb = lib.ndt_tensor_f64_from_data(ctypes.cast(pb.data_ptr(), dp), pb.numel(), shp, 3, ctypes.byref(st))
+        tc = lib.ndt_tensor_f64_contract(ta, la, 3, tb, lb, 3, ctypes.byref(st))
+        assert st.value == 0 and lib.ndt_tensor_f64_data(tc)
+        for t in (ta, tb, tc):
+            lib.ndt_tensor_f64_release(t)
+
+    ms = wall(c1, 20)
+    res["c1 MPS merge"] = {"value": 2.0 * 1024 * 1024 * 256 / (ms * 1e-3) / 1e12, "ms": ms,
+                           "h2d_bytes_per_step": 2 * a.nbytes, "d2h_bytes_per_step": 1024 * 1024 * 8,
+                           "path": "from_data x2 -> ndt_tensor_f64_contract -> data"}
+    # ---- c3: DMRG chain, bond 1024, through contract_gemm
+    host = [pinned(x).numpy().reshape(x.shape, order="F") for x in W.cfg3_tensors(1024)]
+    flops3 = sum(W.cfg3_flops(1024))
+
+    def c3():
+        ts = [ndt.TensorF64.from_numpy(x) for x in host]
+        cur = ts[0]
+        for (la3, lb3), t in zip(W.CFG3_STEPS, ts[1:]):
+            cur = ndt.contract_gemm(cur, la3, t, lb3)
+        assert lib.ndt_tensor_f64_data(cur._ptr)
+
+    ms = wall(c3, 5)
+    res["c3 DMRG chain"] = {"value": flops3 / (ms * 1e-3) / 1e12, "ms": ms,
+                            "h2d_bytes_per_step": sum(x.nbytes for x in host),
+                            "d2h_bytes_per_step": 1024 * 2 * 2 * 1024 * 8,
+                            "path": "from_data x5 -> contract_gemm x4 -> data"}
+    # ---- c5: c128 two-site MPS (A.S).B, bond 8192
+    (sa, ca, a5), (ss, cs5, sd), (sb, cb, b5) = W.cfg5_tensors()
+    pa5, pb5 = pinned(a5).numpy(), pinned(b5).numpy()
+    flops5 = W.flops_blocksparse((sa, ca, None), [1, 2, -1], (sb, cb, None), [-1, 3, 4], True)
+    bs = ndt.blocksparse
+    out_bytes = []
+
+    def c5():
+        A = bs.BlockSparseC64.from_blocks(sa, ca, pa5)
+        S = bs.DiagBlockSparseC64.from_blocks(ss, cs5, sd)
+        B = bs.BlockSparseC64.from_blocks(sb, cb, pb5)
+        C = bs.contract_through_diag(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4])
+        assert lib.ndt_blocksparse_c64_data(C._ptr)
+        out_bytes.append(C.nnz * 16)
+
+    ms = wall(c5, 5)
+    res["c5 c128 MPS"] = {"value": flops5 / (ms * 1e-3) / 1e12, "ms": ms,
+                          "h2d_bytes_per_step": pa5.nbytes + pb5.nbytes + sd.nbytes,
+                          "d2h_bytes_per_step": out_bytes[-1],
+                          "path": "from_data (A, S, B) -> contract_through_diag -> data"}
+    return res
 
 
 def run_extras(args, torch, lib, ndt, stream, peaks):
@@ -878,7 +1113,7 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     torch.cuda.synchronize()
     per = e0.elapsed_time(e1) / (reps * src.shape[0])
     gbs = 2 * NELEM * 16 / (per * 1e-3) / 1e9
-    out.append({"workload": "permutedims 16^6 c128 perm (5,3,1,0,4,2)", "value": gbs, "unit": "GB/s",
+    out.append({"cfg": "c2 permute c128", "workload": "permutedims 16^6 c128 perm (5,3,1,0,4,2)", "value": gbs, "unit": "GB/s",
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                              "frac": gbs / peaks["hbm_gbs"], "traffic": ncu_traffic("permute_16p6_c128")}})
     del src, dst
@@ -940,7 +1175,7 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
     # 64x64 tiles of four 32x32 warp tiles; FP64 MMA throughput is per SM sub-partition (4 per SM)
     tiles, parts = (m // 64) * (n // 64), torch.cuda.get_device_properties(0).multi_processor_count * 4
-    out.append({"workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
+    out.append({"cfg": "c1 MPS merge", "workload": "contract A[256,4,256] x B[256,4,256] -> C[256,4,4,256] f64 (MPS merge)",
                 "value": tf, "unit": "TFLOP/s", "ms": t,
                 "timing": f"{NM} independent merges back to back per event pair, L2 flushed before each stream",
                 "single_launch_ms": statistics.mean(single),
@@ -968,7 +1203,7 @@ def run_extras(args, torch, lib, ndt, stream, peaks):
     torch.cuda.synchronize()
     t = a.elapsed_time(b) / 5
     tf = 2.0 * m * n * k / (t * 1e-3) / 1e12
-    out.append({"workload": "f64 GEMM 4096^3 (DMMA kernel steady state)", "value": tf, "unit": "TFLOP/s",
+    out.append({"cfg": "gemm 4096^3", "workload": "f64 GEMM 4096^3 (DMMA kernel steady state)", "value": tf, "unit": "TFLOP/s",
                 "roofline": fp64_roofline(tf)})
     return out
 
@@ -1028,13 +1263,26 @@ def run_dmrg(args, torch, ndt, peaks, world=1, rank=0, pg=None):
         tot.append(ev[0][0].elapsed_time(ev[3][1]))
     ms = [statistics.median(x) for x in step_ms]
     chain_ms = statistics.median(tot)
+    # this rank's result against the same chain on the host (torch CPU
+    # einsum in float64 over the rank's slab of L)
+    _host_threads(torch, world)
+    got = chain().to_numpy()
+    tL, tpsi, tW1, tW2, tR = (torch.from_numpy(x) for x in host)
+    t1 = torch.einsum("abx,xcde->abcde", tL, tpsi)
+    t2 = torch.einsum("axyde,xfyg->adefg", t1, tW1)
+    t3 = torch.einsum("aycxe,xfyg->acefg", t2, tW2)
+    want = torch.einsum("axbyc,dyx->abcd", t3, tR).numpy()
+    err = float(np.linalg.norm(got - want) / np.linalg.norm(want))
+    par = {"tol": 1e-12, "rel_err": err, "ok": bool(err <= 1e-12),
+           "reference": "torch CPU float64 einsum of the four steps on this rank's slab"}
     if pg:  # max over ranks
         t = torch.tensor(ms + [chain_ms], device="cuda")
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         vals = t.tolist()
         ms, chain_ms = vals[:4], vals[4]
     skinny_bytes = 2 * (2 * D * D) * 10 * 8 + 100 * 8  # read 2D^2 x 10, write 2D^2 x 10, W
-    out = {"workload": "DMRG environment chain L[1024,5,1024].psi[1024,2,2,1024].W1.W2.R[1024,5,1024] f64, "
+    out = {"cfg": "c3 DMRG chain", "parity": par,
+           "workload": "DMRG environment chain L[1024,5,1024].psi[1024,2,2,1024].W1.W2.R[1024,5,1024] f64, "
                        "contract_gemm x4" + (f", split along a over {world} ranks" if world > 1 else ""),
            "value": sum(flops) / (chain_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": chain_ms, "flop": sum(flops),
            "n_gpus": world, "scaling": "strong" if world > 1 else None, "steps": []}
@@ -1069,7 +1317,7 @@ def run_dmrg(args, torch, ndt, peaks, world=1, rank=0, pg=None):
             tn.append(e0.elapsed_time(e1))
         net_ms = statistics.median(tn)
         tf = sum(flops) / (net_ms * 1e-3) / 1e12
-        res.append({"workload": "DMRG environment update as one network (contract_network: W1.W2 fused into one "
+        res.append({"cfg": "c3 DMRG network", "workload": "DMRG environment update as one network (contract_network: W1.W2 fused into one "
                                 "skinny pass), bond 1024", "value": tf, "unit": "TFLOP/s", "ms": net_ms,
                     "flop": sum(flops), "roofline": fp64_roofline(tf)})
     return res

@@ -353,12 +353,15 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_contract_through_diag(
  * output are caller-owned device buffers (column-major, A and B dense over
  * their shapes, zero extents rejected with NDT_INTERNAL_ERROR); c must hold
  * c_len >= output length elements; out_shape (may be NULL) receives the
- * output shape (up to ndim_a + ndim_b entries, or 1).  Operands that need
- * packing use a fixed 16 MiB scratch array in device memory, held by every
- * GPU that loads the library until exit; larger requests are rejected with
- * NDT_INVALID_ARGUMENT (message in ndt_b200_last_error).  The first call on a
- * device looks up that array's device address (make it before any stream
- * capture).  Calls share the array: calls that overlap on the GPU race. */
+ * output shape (up to ndim_a + ndim_b entries, or 1).  An operand whose axes
+ * form a unit-stride strided matrix is read in place at any size; one that
+ * needs packing is packed into a fixed 16 MiB scratch array in device memory,
+ * held by every GPU that loads the library until exit.  Contractions whose
+ * packed operands need more are rejected with NDT_INVALID_ARGUMENT (message in
+ * ndt_b200_last_error).  The first call on a device creates the library's
+ * streams there and looks up that array's device address (make it before any
+ * stream capture); it leaves the device's memory pools and their settings
+ * untouched.  Calls share the array: calls that overlap on the GPU race. */
 int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shape_a, size_t ndim_a, const long* labels_a,
                                   const double* b, const size_t* shape_b, size_t ndim_b, const long* labels_b,
                                   double* c, size_t c_len, size_t* out_shape, size_t* out_ndim, void* stream);

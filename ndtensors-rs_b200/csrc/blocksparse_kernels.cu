@@ -135,7 +135,7 @@ Tables upload(const std::vector<int64_t>& offs, const std::vector<BsBlockDesc>& 
   memcpy(h.data(), offs.data(), b1);
   memcpy(h.data() + o2, blocks.data(), blocks.size() * sizeof(BsBlockDesc));
   void* d = nullptr;
-  NDT_CUDA(cudaMallocAsync(&d, total ? total : 16, s));
+  d = (decltype(d))pool_alloc(total, s);
   NDT_CUDA(cudaMemcpyAsync(d, h.data(), total, cudaMemcpyHostToDevice, s));
   return Tables{(int64_t*)d, (BsBlockDesc*)((char*)d + o2), d};
 }
@@ -188,7 +188,7 @@ void copy_segments(const void* src, void* dst, const std::vector<int64_t>& src_o
   if ((((uintptr_t)src) | ((uintptr_t)dst)) & 15) throw Error(ErrKind::Panic, "copy_segments: base not 16-byte aligned");
   CopySeg* d = nullptr;
   const size_t tb = h.size() * sizeof(CopySeg);
-  NDT_CUDA(cudaMallocAsync((void**)&d, tb, s));
+  d = (decltype(d))pool_alloc(tb, s);
   NDT_CUDA(cudaMemcpyAsync(d, h.data(), tb, cudaMemcpyHostToDevice, s));
   const DeviceCtx& c = ctx();
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items, (int64_t)c.sm_count * 8));
@@ -242,7 +242,7 @@ void bs_diag_scale(DType dt, const void* a, const void* sdiag, void* out, const 
   }
   DiagCols* dt_tab = nullptr;
   const size_t bytes = h.size() * sizeof(DiagCols);
-  NDT_CUDA(cudaMallocAsync((void**)&dt_tab, bytes, s));
+  dt_tab = (decltype(dt_tab))pool_alloc(bytes, s);
   NDT_CUDA(cudaMemcpyAsync(dt_tab, h.data(), bytes, cudaMemcpyHostToDevice, s));
   const DeviceCtx& c = ctx();
   const int64_t want = (ncols * 32 + kThreads - 1) / kThreads;

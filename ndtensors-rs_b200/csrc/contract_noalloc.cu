@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <mutex>
+#include <string>
 
 #include "../../include/ndtensors_capi.h"
 #include "ndt_internal.h"
@@ -76,15 +77,27 @@ bool merge(const std::vector<Ax1>& v, int64_t* stride, bool* empty) {
   return ok;
 }
 
-// Describe one operand for the GEMM, packing it into `scratch` when its axes
-// do not form a unit-stride strided matrix.  `rows` are the M (or N) axes.
-GemmOperand operand(const double* base, const std::vector<Ax1>& rows, const std::vector<Ax1>& cols, int64_t r_ext,
-                    int64_t c_ext, double* scratch, cudaStream_t s) {
+// How one operand reaches the GEMM: read in place when its axes form a
+// unit-stride strided matrix (either orientation), else packed.
+struct Layout {
+  bool pack;
+  bool kmajor;
+  int64_t ld;
+};
+Layout layout(const std::vector<Ax1>& rows, const std::vector<Ax1>& cols, int64_t r_ext, int64_t c_ext) {
   int64_t rs, cs;
   bool re, ce;
   bool rok = merge(rows, &rs, &re), cok = merge(cols, &cs, &ce);
-  if (rok && cok && (re || rs == 1)) return GemmOperand{base, ce ? std::max<int64_t>(r_ext, 1) : cs, false};
-  if (rok && cok && (ce || cs == 1)) return GemmOperand{base, re ? std::max<int64_t>(c_ext, 1) : rs, true};
+  if (rok && cok && (re || rs == 1)) return Layout{false, false, ce ? std::max<int64_t>(r_ext, 1) : cs};
+  if (rok && cok && (ce || cs == 1)) return Layout{false, true, re ? std::max<int64_t>(c_ext, 1) : rs};
+  return Layout{true, false, std::max<int64_t>(r_ext, 1)};
+}
+
+// Describe one operand for the GEMM, packing it into `scratch` when its
+// layout says so.  `rows` are the M (or N) axes.
+GemmOperand operand(const double* base, const std::vector<Ax1>& rows, const std::vector<Ax1>& cols,
+                    const Layout& L, double* scratch, cudaStream_t s) {
+  if (!L.pack) return GemmOperand{base, L.ld, L.kmajor};
   GatherDesc g;
   for (const Ax1& a : rows) {
     g.shape.push_back((size_t)a.n);
@@ -99,7 +112,7 @@ GemmOperand operand(const double* base, const std::vector<Ax1>& rows, const std:
   } else {
     gather(DType::F64, base, scratch, g, s);
   }
-  return GemmOperand{scratch, std::max<int64_t>(r_ext, 1), false};
+  return GemmOperand{scratch, L.ld, false};
 }
 
 }  // namespace
@@ -117,10 +130,17 @@ extern "C" int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shap
     double* scratch = (double*)scratch_address(dev);
     cudaStream_t s = (cudaStream_t)stream;
     std::vector<size_t> sa(shape_a, shape_a + ndim_a), sb(shape_b, shape_b + ndim_b);
+    // Zero extents: the reference panics (linear_to_cartesian divides by them).
     for (size_t x : sa)
-      if (x == 0) return NDT_INTERNAL_ERROR;  // zero extents: the reference panics (linear_to_cartesian)
+      if (x == 0) {
+        set_last_error("ndt_b200_contract_f64_noalloc: A has a zero extent");
+        return NDT_INTERNAL_ERROR;
+      }
     for (size_t x : sb)
-      if (x == 0) return NDT_INTERNAL_ERROR;
+      if (x == 0) {
+        set_last_error("ndt_b200_contract_f64_noalloc: B has a zero extent");
+        return NDT_INTERNAL_ERROR;
+      }
     std::vector<int32_t> la(ndim_a), lb(ndim_b);
     for (size_t i = 0; i < ndim_a; i++) la[i] = (int32_t)labels_a[i];
     for (size_t j = 0; j < ndim_b; j++) lb[j] = (int32_t)labels_b[j];
@@ -130,7 +150,11 @@ extern "C" int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shap
       if (la[i] >= 0) continue;
       for (size_t j = 0; j < ndim_b; j++)
         if (la[i] == lb[j]) {
-          if (sa[i] != sb[j]) return NDT_SHAPE_MISMATCH;
+          if (sa[i] != sb[j]) {
+            set_last_error("ndt_b200_contract_f64_noalloc: contracted extents differ for label " +
+                           std::to_string(la[i]));
+            return NDT_SHAPE_MISMATCH;
+          }
           pairs.push_back({i, j});
           break;
         }
@@ -167,13 +191,16 @@ extern "C" int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shap
       set_last_error("output buffer too small for the contraction result");
       return NDT_INVALID_ARGUMENT;
     }
-    // Worst case both operands are packed: m*k + k*n doubles of scratch.
-    const size_t need = ((size_t)(m * k) + (size_t)(k * n)) * sizeof(double);
+    // Scratch: only the operands that are packed use it, A's part first,
+    // then B's at the next 256-byte boundary.
+    const Layout lay_a = layout(M, KA, m, k), lay_b = layout(N, KB, n, k);
+    const size_t bytes_a = lay_a.pack ? ((size_t)(m * k) * sizeof(double) + 255) / 256 * 256 : 0;
+    const size_t need = bytes_a + (lay_b.pack ? (size_t)(k * n) * sizeof(double) : 0);
     if (need > kNoAllocScratchBytes) {
       char msg[256];
       snprintf(msg, sizeof(msg),
-               "ndt_b200_contract_f64_noalloc: operands need %zu bytes of scratch, more than the fixed %zu "
-               "bytes this entry point holds; use ndt_tensor_f64_contract",
+               "ndt_b200_contract_f64_noalloc: packing the operands needs %zu bytes of scratch, more than the "
+               "fixed %zu bytes this entry point holds; use ndt_tensor_f64_contract",
                need, kNoAllocScratchBytes);
       set_last_error(msg);
       return NDT_INVALID_ARGUMENT;
@@ -182,9 +209,9 @@ extern "C" int ndt_b200_contract_f64_noalloc(const double* a, const size_t* shap
     if (out_shape)
       for (size_t i = 0; i < oshape.size(); i++) out_shape[i] = oshape[i];
     double* scr_a = scratch;
-    double* scr_b = scratch + (size_t)(m * k);
-    GemmOperand ga = operand(a, M, KA, m, k, scr_a, s);
-    GemmOperand gb = operand(b, N, KB, n, k, scr_b, s);
+    double* scr_b = (double*)((unsigned char*)scratch + bytes_a);
+    GemmOperand ga = operand(a, M, KA, lay_a, scr_a, s);
+    GemmOperand gb = operand(b, N, KB, lay_b, scr_b, s);
     // No split-K: its partial sums would need a workspace from the pool.
     gemm(DType::F64, m, n, k, ga, gb, c, std::max<int64_t>(m, 1), false, s, /*allow_split_k=*/false);
     return NDT_SUCCESS;

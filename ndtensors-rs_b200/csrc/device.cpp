@@ -64,18 +64,36 @@ DeviceCtx& ctx(int device) {
   int optin = 0;
   NDT_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
   c->smem_optin = (size_t)optin;
-  // Keep freed device memory in the pool for reuse instead of releasing it
-  // at every synchronisation point.
-  cudaMemPool_t pool;
-  NDT_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
-  uint64_t thresh = UINT64_MAX;
-  NDT_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thresh));
   NDT_CUDA(cudaSetDevice(prev));
   g_ctx[device] = c;
   return *c;
 }
 
 DeviceCtx& ctx() { return ctx(current_device()); }
+
+// Keep freed device memory in the device's default pool for reuse instead of
+// releasing it at every synchronisation point.  Set on the library's first
+// allocation on a device (not when its context is created), so a caller that
+// only uses the allocation-free entry point leaves the pool's release
+// threshold as it found it.
+static void tune_pool(DeviceCtx& c) {
+  if (c.pool_tuned.load(std::memory_order_acquire)) return;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (c.pool_tuned.load(std::memory_order_relaxed)) return;
+  cudaMemPool_t pool;
+  NDT_CUDA(cudaDeviceGetDefaultMemPool(&pool, c.device));
+  uint64_t thresh = UINT64_MAX;
+  NDT_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thresh));
+  c.pool_tuned.store(true, std::memory_order_release);
+}
+
+void* pool_alloc(size_t bytes, cudaStream_t s) {
+  DeviceCtx& c = ctx();
+  tune_pool(c);
+  void* p = nullptr;
+  NDT_CUDA(cudaMallocAsync(&p, bytes ? bytes : 16, s));
+  return p;
+}
 
 void settle_for_caller(int device) {
   DeviceCtx& c = ctx(device);
@@ -84,6 +102,7 @@ void settle_for_caller(int device) {
 
 void* dev_alloc(size_t bytes, int device) {
   DeviceCtx& c = ctx(device);
+  tune_pool(c);
   void* p = nullptr;
   size_t b = bytes ? bytes : 16;
   NDT_CUDA(cudaMallocAsync(&p, b, c.compute));

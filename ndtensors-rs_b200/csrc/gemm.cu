@@ -591,7 +591,7 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
         segs[sp] = GroupedSegment{A.kmajor ? k0 : k0 * A.ld, B.kmajor ? k0 : k0 * B.ld, k1 - k0, A.ld, B.ld, -1};
       }
       void* w = nullptr;
-      NDT_CUDA(cudaMallocAsync(&w, (size_t)S * m * n * esize(dt), s));
+      w = pool_alloc((size_t)S * m * n * esize(dt), s);
       grouped_gemm(dt, A.ptr, B.ptr, w, A.kmajor, B.kmajor, probs, segs, nullptr, s);
       splitk_reduce(dt, w, S, m, n, Cp, ldc, accumulate, s);
       NDT_CUDA(cudaFreeAsync(w, s));
@@ -689,7 +689,7 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   memcpy(host.data() + off_s, segs.data(), bsg);
   memcpy(host.data() + off_t, tiles.data(), bt);
   char* d = nullptr;
-  NDT_CUDA(cudaMallocAsync((void**)&d, total, s));
+  d = (char*)pool_alloc(total, s);
   NDT_CUDA(cudaMemcpyAsync(d, host.data(), total, cudaMemcpyHostToDevice, s));
   KArgs a{};
   a.A = A;

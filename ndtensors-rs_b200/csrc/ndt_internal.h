@@ -25,6 +25,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 #include <memory>
@@ -82,6 +83,7 @@ struct DeviceCtx {
   bool external_stream = false;    // compute stream supplied by the caller
   int sm_count = 0;
   size_t smem_optin = 0;
+  std::atomic<bool> pool_tuned{false};  // default pool's release threshold raised
 };
 DeviceCtx& ctx(int device);
 DeviceCtx& ctx();  // current device
@@ -96,6 +98,8 @@ void settle_for_caller(int device);
 // Device memory: stream-ordered allocations from the device's default pool
 // (release threshold raised so freed blocks are reused, not returned).
 void* dev_alloc(size_t bytes, int device);
+// A stream-ordered allocation on stream `s` from the current device's pool.
+void* pool_alloc(size_t bytes, cudaStream_t s);
 void dev_free(void* p, int device);
 // Pinned host memory with a size-bucketed cache (host mirrors, staging).
 void* pinned_alloc(size_t bytes, bool* pinned);

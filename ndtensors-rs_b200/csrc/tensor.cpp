@@ -191,8 +191,7 @@ Dense make_from_host(DType dt, const void* data, size_t len, const std::vector<s
     int d = current_device();
     DeviceCtx& c = ctx(d);
     s.device = d;
-    void* p = nullptr;
-    NDT_CUDA(cudaMallocAsync(&p, s.bytes() ? s.bytes() : 16, c.upload));
+    void* p = pool_alloc(s.bytes(), c.upload);
     s.dev = p;
     cudaEvent_t ev;
     NDT_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));

@@ -6,9 +6,12 @@ operands into a fixed scratch array compiled into the library instead of
 calling cudaMalloc.  This test calls it through the C ABI on caller-owned
 device buffers and compares the result with ndt_tensor_f64_contract on the
 same inputs, on two calls in a row (the scratch array keeps the previous
-call's contents, which must not leak into the next result), and checks through
+call's contents, which must not leak into the next result), and with the
+oracle's restatement of the reference's naive contraction; it checks through
 the device's default memory pool (the one the library allocates from) that a
-call takes no memory from it.  The file name makes pytest collect it last.
+call takes no memory from it.  Only operands that need packing count against
+the scratch limit: a contraction whose operands are read in place runs at any
+size.  The file name makes pytest collect it last.
 """
 
 from __future__ import annotations
@@ -62,29 +65,57 @@ CASES = [
 ]
 
 
+def _seed(*key):
+    return int.from_bytes(repr(key).encode(), "little") % (2**32)
+
+
 @pytest.mark.parametrize("sa,la,sb,lb", CASES)
-def test_noalloc_matches_regular_entry_point(gpu, sa, la, sb, lb):
+def test_noalloc_matches_regular_entry_point(gpu, oracle, sa, la, sb, lb):
     import torch
 
     lib = gpu.get_lib()
-    rng = np.random.default_rng(abs(hash((sa, la, sb, lb))) % (2**32))
+    rng = np.random.default_rng(_seed(sa, la, sb, lb))
     a, b = rng.standard_normal(sa), rng.standard_normal(sb)
     ref = gpu.contract(gpu.TensorF64.from_numpy(a), la, gpu.TensorF64.from_numpy(b), lb).to_numpy()
+    ost, oref = oracle.contract_naive(a, list(la), b, list(lb))
+    assert ost == 0 and oref.shape == ref.shape
     for _ in range(2):  # two calls in a row share the scratch array
         st, got = _noalloc(lib, torch, a, list(la), b, list(lb), ref.size)
         assert st == 0, gpu.last_error()
         assert got.shape == ref.shape
         assert rel_fro(got, ref) <= RTOL
+        assert rel_fro(got, oref) <= RTOL
+
+
+def test_noalloc_unpacked_operands_have_no_size_limit(gpu):
+    """A (2048 x 1024, 16 MiB) is read in place as an MN-major matrix and B
+    (1024 x 96) as a K-major one: nothing is packed, so the call succeeds
+    although the two operands together exceed the scratch array."""
+    import torch
+
+    lib = gpu.get_lib()
+    rng = np.random.default_rng(11)
+    a, b = rng.standard_normal((2048, 1024)), rng.standard_normal((1024, 96))
+    ref = gpu.contract(gpu.TensorF64.from_numpy(a), [1, -1], gpu.TensorF64.from_numpy(b), [-1, 2]).to_numpy()
+    want = a @ b
+    assert a.nbytes + b.nbytes > 16 << 20
+    for _ in range(2):
+        st, got = _noalloc(lib, torch, a, [1, -1], b, [-1, 2], ref.size)
+        assert st == 0, gpu.last_error()
+        assert rel_fro(got, ref) <= RTOL
+        assert rel_fro(got, want) <= RTOL
 
 
 def test_noalloc_rejects_oversize_scratch(gpu):
     import torch
 
     lib = gpu.get_lib()
-    # packing A (3M doubles = 24 MB) exceeds the fixed 16 MiB scratch
-    a = np.zeros((3000, 1000))
-    b = np.zeros((3000, 2))
-    st, _ = _noalloc(lib, torch, a, [-1, 1], b, [-1, 2], 2000)
+    # A's contracted axes (labels -2 on axis 0, -1 on axis 2) are not one
+    # strided run in pair order, so A is packed: m * k = 300 * 10000 doubles
+    # (24 MB), more than the fixed 16 MiB scratch.
+    a = np.zeros((40, 300, 250))
+    b = np.zeros((250, 40, 2))
+    st, _ = _noalloc(lib, torch, a, [-2, 1, -1], b, [-1, -2, 2], 600)
     assert st == -1
     assert "scratch" in gpu.last_error()
 
