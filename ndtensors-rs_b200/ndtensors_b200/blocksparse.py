@@ -374,11 +374,20 @@ def shard_plan(a, labels_a, b, labels_b, nranks: int):
 
 
 class _DeviceSpan:
-    """A raw device range exposed through __cuda_array_interface__ (zero copy)."""
+    """A raw device range exposed through __cuda_array_interface__ (zero copy).
+
+    Version 3 with the library's compute stream as "stream": a consumer (torch)
+    makes its own stream wait for the library's work on the range before it
+    touches it.  device_ptr / device_ptr_mut already return with that work
+    complete when the library runs on its own stream; with a caller stream
+    installed (ndt_b200_set_stream) the key orders the two streams."""
 
     def __init__(self, ptr: int, n: int):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f8", "data": (int(ptr), False),
-                                         "strides": None, "version": 2}
+        lib_stream = get_lib().ndt_b200_get_stream() or 0
+        cai = {"shape": (n,), "typestr": "<f8", "data": (int(ptr), False), "strides": None, "version": 3}
+        if lib_stream:
+            cai["stream"] = int(lib_stream)
+        self.__cuda_array_interface__ = cai
 
 
 _HOST_GROUPS = {}
