@@ -28,6 +28,8 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <queue>
 #include <vector>
 
@@ -50,6 +52,7 @@ struct KArgs {
   const void* kscale;  // grouped mode: per-k scale (segments' scale_off), or null
   int kscale_real;     // complex scale values whose imaginary parts are all zero
   int accumulate;
+  int ntiles;          // grouped mode: entries of `tiles`
 };
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
@@ -450,6 +453,362 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
       }
 }
 
+
+// Persistent grouped kernel (block-sparse contractions, split-K pieces).
+// gridDim.x CTAs, at most as many as fit on the GPU at once, walk the tile
+// list (heaviest first) in snake order: CTA b takes tiles b, 2G-1-b, 2G+b,
+// ... (G = gridDim.x), so every round hands the heaviest remaining tiles to
+// the CTAs that got the lightest ones in the round before.  The cp.async
+// ring runs across tile boundaries: while a tile's last k-steps and its
+// epilogue execute, the next tile's first stages are already in flight, so
+// the pipeline fills once per CTA rather than once per tile.  Tiles of short,
+// ragged blocks (most of a block-sparse contraction) are where that fill
+// would otherwise be paid again and again.
+// Warp fragments that lie wholly outside the output block (rows >= m or
+// columns >= n) and k8 steps past the end of a segment issue no MMA: those
+// products are zero.  On ragged blocks that saves the padded part of the
+// edge tiles (the c128 MPS chain: 86% useful work at 32 x 64 tile
+// granularity, 96% at the 16 x 8 x 8 MMA granularity).
+template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
+          int SCALE>
+__global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
+    dmma_grouped_kernel(const __grid_constant__ KArgs args) {
+  pdl_release();
+  pdl_wait();  // before the first global access (tile tables, operands)
+  using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM, SCALE>;
+  constexpr int NTH = C::kThreads, MT = C::MT, NT = C::NT, ES = C::ES;
+  constexpr int LDA = C::PA::value, LDB = C::PB::value;
+  constexpr int RPL = CPLX ? 2 : 1;  // doubles per element
+  constexpr int PW = (!CPLX && VEC) ? 2 : 1;
+  using PlanA = CopyPlan<AK ? BM : BK, AK ? BK : BM, PW, NTH>;
+  using PlanB = CopyPlan<BKM ? BN : BK, BKM ? BK : BN, PW, NTH>;
+  extern __shared__ __align__(16) double smem[];
+  __shared__ int s_kvalid[STAGES];  // k rows of each staged k-step that lie inside its segment
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  const int wm0 = (warp % WM_WARPS) * C::WM;
+  const int wn0 = (warp / WM_WARPS) * C::WN;
+  const int G = gridDim.x, cta = blockIdx.x, ntiles = args.ntiles;
+  auto tile_of = [&](int i) -> int { return i * G + ((i & 1) ? (G - 1 - cta) : cta); };
+
+  const char* Ab = (const char*)args.A;
+  const char* Bb = (const char*)args.B;
+  // per-thread copy geometry (constant over the launch)
+  const int a_c = (tid % PlanA::CW) * PW, a_r = tid / PlanA::CW;
+  const int b_c = (tid % PlanB::CW) * PW, b_r = tid / PlanB::CW;
+
+  // ---- load side: the tile whose stages are being issued, and (segment, k0) within it
+  int l_i = 0;
+  int64_t l_m0 = 0, l_n0 = 0, a_mrem = 0, b_nrem = 0;
+  int64_t seg = 0, seg_end = 0, a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0, s_off = 0;
+  auto load_seg = [&](int64_t sidx) {
+    const GroupedSegment sd = args.segs[sidx];
+    a_off = sd.a_off;
+    b_off = sd.b_off;
+    kseg = sd.k;
+    lda = sd.lda;
+    ldb = sd.ldb;
+    s_off = sd.scale_off;
+  };
+  // Set the load side up on tile_of(l_i) or the first later tile with a
+  // non-empty segment; false when the CTA has no tiles left to load.
+  auto load_tile = [&]() -> bool {
+    for (int ti = tile_of(l_i); ti < ntiles; ti = tile_of(++l_i)) {
+      const int4 td = args.tiles[ti];
+      const GroupedProblem pr = args.probs[td.x];
+      seg = pr.seg_begin;
+      seg_end = pr.seg_begin + pr.seg_count;
+      while (seg < seg_end && args.segs[seg].k <= 0) seg++;
+      if (seg < seg_end) {
+        l_m0 = (int64_t)td.y * BM;
+        l_n0 = (int64_t)td.z * BN;
+        a_mrem = pr.m - l_m0;
+        b_nrem = pr.n - l_n0;
+        k0 = 0;
+        load_seg(seg);
+        return true;
+      }
+    }
+    return false;
+  };
+  bool loading = load_tile();
+  auto advance = [&]() {
+    k0 += BK;
+    if (k0 >= kseg) {
+      k0 = 0;
+      seg++;
+      while (seg < seg_end && args.segs[seg].k <= 0) seg++;
+      if (seg < seg_end) {
+        load_seg(seg);
+      } else {
+        l_i++;
+        loading = load_tile();
+      }
+    }
+  };
+  auto issue_load = [&](int stage) {
+    double* As = smem + (size_t)stage * C::stage_elems * RPL;
+    double* Bs = As + (size_t)C::PA::elems * RPL;
+    const int64_t krem = kseg - k0;  // k rows left in this segment
+    if (tid == 0) s_kvalid[stage] = krem < BK ? (int)krem : BK;
+    {
+      const int64_t cont_rem = AK ? krem - a_c : a_mrem - a_c;
+      const int nv = cont_rem >= PW ? PW : (cont_rem > 0 ? (int)cont_rem : 0);
+      const int64_t row_rem = (AK ? a_mrem : krem) - a_r;
+      const char* src =
+          Ab + (a_off + (AK ? (k0 + a_c) + (l_m0 + a_r) * lda : (l_m0 + a_c) + (k0 + a_r) * lda)) * ES;
+      const int64_t rstep = (int64_t)PlanA::RS * lda * ES;
+      double* dst = As + ((size_t)a_r * LDA + a_c) * RPL;
+#pragma unroll
+      for (int it = 0; it < PlanA::IT; it++) {
+        const bool rok = it * PlanA::RS < row_rem;
+        const int nb = rok ? nv : 0;
+        const char* p = nb ? src + it * rstep : Ab;
+        double* d = dst + (size_t)it * PlanA::RS * LDA * RPL;
+        if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
+        else if constexpr (CPLX)
+          cp_async16n(d, p, nb * 16);
+        else
+          cp_async8(d, p, nb != 0);
+      }
+    }
+    {
+      const int64_t cont_rem = BKM ? krem - b_c : b_nrem - b_c;
+      const int nv = cont_rem >= PW ? PW : (cont_rem > 0 ? (int)cont_rem : 0);
+      const int64_t row_rem = (BKM ? b_nrem : krem) - b_r;
+      const char* src =
+          Bb + (b_off + (BKM ? (k0 + b_c) + (l_n0 + b_r) * ldb : (l_n0 + b_c) + (k0 + b_r) * ldb)) * ES;
+      const int64_t rstep = (int64_t)PlanB::RS * ldb * ES;
+      double* dst = Bs + ((size_t)b_r * LDB + b_c) * RPL;
+#pragma unroll
+      for (int it = 0; it < PlanB::IT; it++) {
+        const bool rok = it * PlanB::RS < row_rem;
+        const int nb = rok ? nv : 0;
+        const char* p = nb ? src + it * rstep : Bb;
+        double* d = dst + (size_t)it * PlanB::RS * LDB * RPL;
+        if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
+        else if constexpr (CPLX)
+          cp_async16n(d, p, nb * 16);
+        else
+          cp_async8(d, p, nb != 0);
+      }
+    }
+    if constexpr (SCALE != 0) {
+      double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
+      if (tid < BK) {
+        const bool ok = tid < krem;
+        const char* src = (const char*)args.kscale + (s_off + (ok ? k0 + tid : 0)) * ES;
+        if constexpr (CPLX)
+          cp_async16n(Ss + tid * 2, src, ok ? 16 : 0);
+        else
+          cp_async8(Ss + tid, src, ok);
+      }
+    }
+  };
+
+  // ---- compute side: the tile whose k-steps are being computed
+  constexpr int PLANES = CPLX ? 3 : 1;
+  double acc[MT][NT][4 * PLANES];
+#pragma unroll
+  for (int i = 0; i < MT; i++)
+#pragma unroll
+    for (int j = 0; j < NT; j++)
+#pragma unroll
+      for (int q = 0; q < 4 * PLANES; q++) acc[i][j][q] = 0.0;
+  int c_i = 0, csteps = 0;
+  int64_t cm = 0, cn = 0, c_off = 0, cm0 = 0, cn0 = 0;
+  int mrows = 0, ncols = 0;  // rows / columns of this warp's tile that lie in the block
+  // C tile (+)= acc for the compute tile; clears acc.
+  auto epilogue = [&]() {
+    char* Cb = (char*)args.C + c_off * ES;
+#pragma unroll
+    for (int i = 0; i < MT; i++)
+#pragma unroll
+      for (int j = 0; j < NT; j++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const int64_t row = cm0 + wm0 + i * 16 + g + 8 * (q >> 1);
+          const int64_t col = cn0 + wn0 + j * 8 + 2 * t + (q & 1);
+          if (row < cm && col < cn) {
+            if constexpr (CPLX) {
+              double2* p = reinterpret_cast<double2*>(Cb) + (row + col * cm);
+              const double x = acc[i][j][q], y = acc[i][j][4 + q], z = acc[i][j][8 + q];
+              double2 v = make_double2(x - y, z - x - y);
+              if (args.accumulate) {
+                const double2 o = *p;
+                v.x += o.x;
+                v.y += o.y;
+              }
+              *p = v;
+            } else {
+              double* p = reinterpret_cast<double*>(Cb) + (row + col * cm);
+              double v = acc[i][j][q];
+              if (args.accumulate) v += *p;
+              *p = v;
+            }
+          }
+#pragma unroll
+          for (int pl = 0; pl < PLANES; pl++) acc[i][j][4 * pl + q] = 0.0;
+        }
+  };
+  // Set the compute side up on tile_of(c_i) or the first later tile with
+  // k-steps; tiles without any are written as zeros on the way.  False when
+  // the CTA's tiles are done.
+  auto compute_tile = [&]() -> bool {
+    for (int ti = tile_of(c_i); ti < ntiles; ti = tile_of(++c_i)) {
+      const int4 td = args.tiles[ti];
+      const GroupedProblem pr = args.probs[td.x];
+      cm = pr.m;
+      cn = pr.n;
+      c_off = pr.c_off;
+      cm0 = (int64_t)td.y * BM;
+      cn0 = (int64_t)td.z * BN;
+      const int64_t mr = cm - cm0 - wm0, nc = cn - cn0 - wn0;
+      mrows = mr < 0 ? 0 : (mr > C::WM ? C::WM : (int)mr);
+      ncols = nc < 0 ? 0 : (nc > C::WN ? C::WN : (int)nc);
+      csteps = 0;
+      for (int64_t sidx = pr.seg_begin; sidx < pr.seg_begin + pr.seg_count; sidx++) {
+        const int64_t kk = args.segs[sidx].k;
+        if (kk > 0) csteps += (int)((kk + BK - 1) / BK);
+      }
+      if (csteps > 0) return true;
+      epilogue();  // no k-steps: the block's tile is zero
+    }
+    return false;
+  };
+
+  // ---- prologue
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; s++) {
+    if (loading) {
+      issue_load(s);
+      advance();
+    }
+    cp_commit();
+  }
+
+  bool active = compute_tile();
+  int cs = 0, ls = STAGES - 1;  // stage computed / stage loaded
+  while (active) {
+    cp_wait<STAGES - 2>();
+    __syncthreads();
+    if (loading) {
+      issue_load(ls);
+      advance();
+    }
+    cp_commit();
+    ls = (ls + 1 == STAGES) ? 0 : ls + 1;
+    const double* As = smem + (size_t)cs * C::stage_elems * RPL;
+    const double* Bs = As + (size_t)C::PA::elems * RPL;
+    const int kval = s_kvalid[cs];
+#pragma unroll
+    for (int kk = 0; kk < BK; kk += 8) {
+      if (kk >= kval) break;  // the rest of this stage is past the segment's end
+      double a[MT][4], b[NT][2];
+      double ai[MT][4], bi[NT][2];
+#pragma unroll
+      for (int i = 0; i < MT; i++) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          int row = wm0 + i * 16 + g + 8 * (q & 1);
+          int col = kk + t + 4 * (q >> 1);
+          int idx = AK ? row * LDA + col : col * LDA + row;
+          if constexpr (CPLX) {
+            double2 v = *reinterpret_cast<const double2*>(As + (size_t)idx * 2);
+            a[i][q] = v.x;
+            ai[i][q] = v.y;
+          } else {
+            a[i][q] = As[idx];
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < NT; j++) {
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          int col = wn0 + j * 8 + g;
+          int kr = kk + t + 4 * q;
+          int idx = BKM ? col * LDB + kr : kr * LDB + col;
+          if constexpr (CPLX) {
+            double2 v = *reinterpret_cast<const double2*>(Bs + (size_t)idx * 2);
+            b[j][q] = v.x;
+            bi[j][q] = v.y;
+          } else {
+            b[j][q] = Bs[idx];
+          }
+        }
+      }
+      if constexpr (SCALE != 0) {
+        // s(k) B(k, j) as the B fragments leave shared memory (see dmma_gemm_kernel)
+        const double* Ss = As + (size_t)(C::PA::elems + C::PB::elems) * RPL;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          const int kr = kk + t + 4 * q;
+          if constexpr (CPLX && SCALE == 2) {
+            const double2 sv = *reinterpret_cast<const double2*>(Ss + (size_t)kr * 2);
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+              const double re = b[j][q], im = bi[j][q];
+              b[j][q] = re * sv.x - im * sv.y;
+              bi[j][q] = re * sv.y + im * sv.x;
+            }
+          } else if constexpr (CPLX) {
+            const double sv = Ss[(size_t)kr * 2];
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+              b[j][q] *= sv;
+              bi[j][q] *= sv;
+            }
+          } else {
+            const double sv = Ss[kr];
+#pragma unroll
+            for (int j = 0; j < NT; j++) b[j][q] *= sv;
+          }
+        }
+      }
+      if constexpr (!CPLX) {
+#pragma unroll
+        for (int i = 0; i < MT; i++)
+#pragma unroll
+          for (int j = 0; j < NT; j++)
+            if (i * 16 < mrows && j * 8 < ncols)
+              dmma(acc[i][j][0], acc[i][j][1], acc[i][j][2], acc[i][j][3], a[i], b[j]);
+      } else {
+        double as[MT][4], bs[NT][2];
+#pragma unroll
+        for (int i = 0; i < MT; i++)
+#pragma unroll
+          for (int q = 0; q < 4; q++) as[i][q] = a[i][q] + ai[i][q];
+#pragma unroll
+        for (int j = 0; j < NT; j++)
+#pragma unroll
+          for (int q = 0; q < 2; q++) bs[j][q] = b[j][q] + bi[j][q];
+#pragma unroll
+        for (int i = 0; i < MT; i++)
+#pragma unroll
+          for (int j = 0; j < NT; j++)
+            if (i * 16 < mrows && j * 8 < ncols) {
+              double* cc = acc[i][j];
+              dmma(cc[0], cc[1], cc[2], cc[3], a[i], b[j]);      // X += Ar Br
+              dmma(cc[4], cc[5], cc[6], cc[7], ai[i], bi[j]);    // Y += Ai Bi
+              dmma(cc[8], cc[9], cc[10], cc[11], as[i], bs[j]);  // Z += (Ar + Ai)(Br + Bi)
+            }
+      }
+    }
+    cs = (cs + 1 == STAGES) ? 0 : cs + 1;
+    if (--csteps == 0) {
+      epilogue();
+      c_i++;
+      active = compute_tile();
+    }
+  }
+  cp_wait<0>();
+}
+
 template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED,
           int SCALE>
 void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
@@ -461,16 +820,45 @@ void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
   NDT_CUDA(cudaGetLastError());
 }
 
+// CTAs of `kern` resident per SM with `threads` threads and `smem` bytes of
+// dynamic shared memory (looked up once per device and kernel).
+int resident_per_sm(const void* kern, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> cache;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find({dev, kern});
+  if (it != cache.end()) return it->second;
+  int nb = 0;
+  NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem));
+  if (nb < 1) nb = 1;
+  cache[{dev, kern}] = nb;
+  return nb;
+}
+
+// Grouped launch: the persistent kernel on min(tiles, resident CTAs) CTAs.
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, int SCALE>
+void launch_grouped(const KArgs& a, cudaStream_t s) {
+  using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, SCALE>;
+  auto kern = dmma_grouped_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, SCALE>;
+  ensure_dynamic_smem((const void*)kern, C::smem_bytes);
+  const int per_sm = resident_per_sm((const void*)kern, C::kThreads, C::smem_bytes);
+  const int grid = (int)std::min<int64_t>(a.ntiles, (int64_t)per_sm * ctx().sm_count);
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
+  count_launch();
+  NDT_CUDA(cudaGetLastError());
+}
+
 template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC>
 void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
   if (a.tiles == nullptr)
     launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, false, 0>(a, grid, s);
   else if (a.kscale == nullptr)
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, 0>(a, grid, s);
+    launch_grouped<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, 0>(a, s);
   else if (!CPLX || a.kscale_real)
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, 1>(a, grid, s);
+    launch_grouped<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, 1>(a, s);
   else
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, true, CPLX ? 2 : 1>(a, grid, s);
+    launch_grouped<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, CPLX ? 2 : 1>(a, s);
 }
 
 // Tile classes, indexed by `cls`, with their steady-state rate relative to
@@ -701,6 +1089,7 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.kscale = kscale;
   a.kscale_real = kscale_real ? 1 : 0;
   a.accumulate = 0;
+  a.ntiles = (int)tiles.size();
   int grid = (int)tiles.size();
   bool vec = aligned16(A) && aligned16(B);
   for (const GroupedSegment& sg : segs)
