@@ -31,6 +31,7 @@
 #include <map>
 #include <mutex>
 #include <queue>
+#include <type_traits>
 #include <vector>
 
 #include "ndt_internal.h"
@@ -53,6 +54,7 @@ struct KArgs {
   int kscale_real;     // complex scale values whose imaginary parts are all zero
   int accumulate;
   int ntiles;          // grouped mode: entries of `tiles`
+  int* counter;        // grouped mode: tile reservation counter (zero at launch)
 };
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
@@ -456,19 +458,26 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
 
 // Persistent grouped kernel (block-sparse contractions, split-K pieces).
 // gridDim.x CTAs, at most as many as fit on the GPU at once, walk the tile
-// list (heaviest first) in snake order: CTA b takes tiles b, 2G-1-b, 2G+b,
-// ... (G = gridDim.x), so every round hands the heaviest remaining tiles to
-// the CTAs that got the lightest ones in the round before.  The cp.async
-// ring runs across tile boundaries: while a tile's last k-steps and its
-// epilogue execute, the next tile's first stages are already in flight, so
-// the pipeline fills once per CTA rather than once per tile.  Tiles of short,
-// ragged blocks (most of a block-sparse contraction) are where that fill
-// would otherwise be paid again and again.
-// Warp fragments that lie wholly outside the output block (rows >= m or
-// columns >= n) and k8 steps past the end of a segment issue no MMA: those
-// products are zero.  On ragged blocks that saves the padded part of the
-// edge tiles (the c128 MPS chain: 86% useful work at 32 x 64 tile
-// granularity, 96% at the 16 x 8 x 8 MMA granularity).
+// list (heaviest first).  CTA b starts on tile b; later tiles come from a
+// counter in the tile table, so each CTA takes the heaviest tile left when it
+// reserves one: greedy list scheduling, as the block scheduler does for a
+// grid of one CTA per tile, which matters when tile costs span orders of
+// magnitude (U(1) blocks).  Thread 0 reserves tiles into a small shared ring
+// up to three ahead of the tile being computed, which covers the tiles whose
+// stages are in flight.  The cp.async ring runs across tile boundaries:
+// while a tile's last k-steps and its epilogue execute, the next tile's
+// first stages are already in flight, so the pipeline fills once per CTA
+// rather than once per tile.  Tiles of short, ragged blocks (most of a
+// block-sparse contraction) are where that fill would otherwise be paid again
+// and again.
+// On edge tiles, warp fragments that lie wholly outside the output block
+// (rows >= m or columns >= n) and k8 steps past the end of a segment issue no
+// MMA: those products are zero.  On ragged blocks that saves the padded part
+// of the edge tiles (the c128 MPS chain: 86% useful work at 32 x 64 tile
+// granularity, 96% at the 16 x 8 x 8 MMA granularity).  Interior k-steps of
+// interior tiles take an unpredicated path.
+// A tile whose block has no contracted extent (all its segments empty) runs
+// one k-step of zeros and writes a zero tile.
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
           int SCALE>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
@@ -484,6 +493,8 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   using PlanB = CopyPlan<BKM ? BN : BK, BKM ? BK : BN, PW, NTH>;
   extern __shared__ __align__(16) double smem[];
   __shared__ int s_kvalid[STAGES];  // k rows of each staged k-step that lie inside its segment
+  constexpr int RING = 8;           // reserved tiles: this CTA's j-th tile is s_ring[j % RING]
+  __shared__ int s_ring[RING];
 
   const int tid = threadIdx.x;
   const int lane = tid & 31, warp = tid >> 5;
@@ -491,7 +502,18 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   const int wm0 = (warp % WM_WARPS) * C::WM;
   const int wn0 = (warp / WM_WARPS) * C::WN;
   const int G = gridDim.x, cta = blockIdx.x, ntiles = args.ntiles;
-  auto tile_of = [&](int i) -> int { return i * G + ((i & 1) ? (G - 1 - cta) : cta); };
+  // Tile reservation.  `produced` (the same on every thread) counts the ring
+  // entries written; thread 0 writes them.  Every entry is written before a
+  // barrier that precedes its first read, and is overwritten only RING
+  // entries later, after its tile's compute has started.
+  int produced = 3;
+  if (tid == 0) {
+    s_ring[0] = cta;
+    s_ring[1] = G + atomicAdd(args.counter, 1);
+    s_ring[2] = G + atomicAdd(args.counter, 1);
+  }
+  __syncthreads();
+  auto tile_of = [&](int j) -> int { return s_ring[j % RING]; };
 
   const char* Ab = (const char*)args.A;
   const char* Bb = (const char*)args.B;
@@ -512,26 +534,29 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     ldb = sd.ldb;
     s_off = sd.scale_off;
   };
-  // Set the load side up on tile_of(l_i) or the first later tile with a
-  // non-empty segment; false when the CTA has no tiles left to load.
+  // Set the load side up on this CTA's l_i-th tile; false when it has no
+  // tiles left.  A tile without a non-empty segment gets one null k-step
+  // (kseg = 0: the stage is zero-filled and computes nothing).
   auto load_tile = [&]() -> bool {
-    for (int ti = tile_of(l_i); ti < ntiles; ti = tile_of(++l_i)) {
-      const int4 td = args.tiles[ti];
-      const GroupedProblem pr = args.probs[td.x];
-      seg = pr.seg_begin;
-      seg_end = pr.seg_begin + pr.seg_count;
-      while (seg < seg_end && args.segs[seg].k <= 0) seg++;
-      if (seg < seg_end) {
-        l_m0 = (int64_t)td.y * BM;
-        l_n0 = (int64_t)td.z * BN;
-        a_mrem = pr.m - l_m0;
-        b_nrem = pr.n - l_n0;
-        k0 = 0;
-        load_seg(seg);
-        return true;
-      }
+    const int ti = tile_of(l_i);
+    if (ti >= ntiles) return false;
+    const int4 td = args.tiles[ti];
+    const GroupedProblem pr = args.probs[td.x];
+    seg = pr.seg_begin;
+    seg_end = pr.seg_begin + pr.seg_count;
+    while (seg < seg_end && args.segs[seg].k <= 0) seg++;
+    l_m0 = (int64_t)td.y * BM;
+    l_n0 = (int64_t)td.z * BN;
+    a_mrem = pr.m - l_m0;
+    b_nrem = pr.n - l_n0;
+    k0 = 0;
+    if (seg < seg_end) {
+      load_seg(seg);
+    } else {
+      seg = seg_end - 1;  // the null step: advance() then moves to the next tile
+      kseg = 0;
     }
-    return false;
+    return true;
   };
   bool loading = load_tile();
   auto advance = [&]() {
@@ -655,30 +680,28 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
           for (int pl = 0; pl < PLANES; pl++) acc[i][j][4 * pl + q] = 0.0;
         }
   };
-  // Set the compute side up on tile_of(c_i) or the first later tile with
-  // k-steps; tiles without any are written as zeros on the way.  False when
-  // the CTA's tiles are done.
+  // Set the compute side up on this CTA's c_i-th tile; false when its
+  // tiles are done.  A tile without k-steps computes the one null step.
   auto compute_tile = [&]() -> bool {
-    for (int ti = tile_of(c_i); ti < ntiles; ti = tile_of(++c_i)) {
-      const int4 td = args.tiles[ti];
-      const GroupedProblem pr = args.probs[td.x];
-      cm = pr.m;
-      cn = pr.n;
-      c_off = pr.c_off;
-      cm0 = (int64_t)td.y * BM;
-      cn0 = (int64_t)td.z * BN;
-      const int64_t mr = cm - cm0 - wm0, nc = cn - cn0 - wn0;
-      mrows = mr < 0 ? 0 : (mr > C::WM ? C::WM : (int)mr);
-      ncols = nc < 0 ? 0 : (nc > C::WN ? C::WN : (int)nc);
-      csteps = 0;
-      for (int64_t sidx = pr.seg_begin; sidx < pr.seg_begin + pr.seg_count; sidx++) {
-        const int64_t kk = args.segs[sidx].k;
-        if (kk > 0) csteps += (int)((kk + BK - 1) / BK);
-      }
-      if (csteps > 0) return true;
-      epilogue();  // no k-steps: the block's tile is zero
+    const int ti = tile_of(c_i);
+    if (ti >= ntiles) return false;
+    const int4 td = args.tiles[ti];
+    const GroupedProblem pr = args.probs[td.x];
+    cm = pr.m;
+    cn = pr.n;
+    c_off = pr.c_off;
+    cm0 = (int64_t)td.y * BM;
+    cn0 = (int64_t)td.z * BN;
+    const int64_t mr = cm - cm0 - wm0, nc = cn - cn0 - wn0;
+    mrows = mr < 0 ? 0 : (mr > C::WM ? C::WM : (int)mr);
+    ncols = nc < 0 ? 0 : (nc > C::WN ? C::WN : (int)nc);
+    csteps = 0;
+    for (int64_t sidx = pr.seg_begin; sidx < pr.seg_begin + pr.seg_count; sidx++) {
+      const int64_t kk = args.segs[sidx].k;
+      if (kk > 0) csteps += (int)((kk + BK - 1) / BK);
     }
-    return false;
+    if (csteps == 0) csteps = 1;
+    return true;
   };
 
   // ---- prologue
@@ -694,6 +717,14 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   bool active = compute_tile();
   int cs = 0, ls = STAGES - 1;  // stage computed / stage loaded
   while (active) {
+    // Keep tiles c_i .. c_i + 3 reserved: this iteration computes a step of
+    // tile c_i, and after issuing its load the load iterator points at the
+    // step STAGES = 3 steps ahead, which (every tile has a step) lies at most
+    // three tiles further on.
+    if (produced < c_i + 4) {
+      if (tid == 0) s_ring[produced % RING] = G + atomicAdd(args.counter, 1);
+      produced++;
+    }
     cp_wait<STAGES - 2>();
     __syncthreads();
     if (loading) {
@@ -705,9 +736,13 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     const double* As = smem + (size_t)cs * C::stage_elems * RPL;
     const double* Bs = As + (size_t)C::PA::elems * RPL;
     const int kval = s_kvalid[cs];
+    // One k-step.  FULL: an interior tile and a whole stage (no predicates,
+    // so the fragment loads of consecutive k8 steps overlap the MMAs).
+    auto kstep = [&](auto full_tag) {
+      constexpr bool FULL = decltype(full_tag)::value;
 #pragma unroll
     for (int kk = 0; kk < BK; kk += 8) {
-      if (kk >= kval) break;  // the rest of this stage is past the segment's end
+      if (!FULL && kk >= kval) continue;  // past the segment's end
       double a[MT][4], b[NT][2];
       double ai[MT][4], bi[NT][2];
 #pragma unroll
@@ -775,7 +810,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
         for (int i = 0; i < MT; i++)
 #pragma unroll
           for (int j = 0; j < NT; j++)
-            if (i * 16 < mrows && j * 8 < ncols)
+            if (FULL || (i * 16 < mrows && j * 8 < ncols))
               dmma(acc[i][j][0], acc[i][j][1], acc[i][j][2], acc[i][j][3], a[i], b[j]);
       } else {
         double as[MT][4], bs[NT][2];
@@ -791,7 +826,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
         for (int i = 0; i < MT; i++)
 #pragma unroll
           for (int j = 0; j < NT; j++)
-            if (i * 16 < mrows && j * 8 < ncols) {
+            if (FULL || (i * 16 < mrows && j * 8 < ncols)) {
               double* cc = acc[i][j];
               dmma(cc[0], cc[1], cc[2], cc[3], a[i], b[j]);      // X += Ar Br
               dmma(cc[4], cc[5], cc[6], cc[7], ai[i], bi[j]);    // Y += Ai Bi
@@ -799,6 +834,11 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
             }
       }
     }
+    };
+    if (kval == BK && mrows == C::WM && ncols == C::WN)
+      kstep(std::true_type{});
+    else
+      kstep(std::false_type{});
     cs = (cs + 1 == STAGES) ? 0 : cs + 1;
     if (--csteps == 0) {
       epilogue();
@@ -1071,7 +1111,8 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment),
          bt = tiles.size() * sizeof(int4);
   size_t off_s = (bp + 255) / 256 * 256, off_t = off_s + (bsg + 255) / 256 * 256;
-  size_t total = off_t + bt;
+  size_t off_c = off_t + (bt + 255) / 256 * 256;  // tile reservation counter, uploaded as zero
+  size_t total = off_c + sizeof(int);
   std::vector<char> host(total);
   memcpy(host.data(), probs.data(), bp);
   memcpy(host.data() + off_s, segs.data(), bsg);
@@ -1084,6 +1125,7 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.B = B;
   a.C = Cp;
   a.tiles = (const int4*)(d + off_t);
+  a.counter = (int*)(d + off_c);
   a.probs = (const GroupedProblem*)d;
   a.segs = (const GroupedSegment*)(d + off_s);
   a.kscale = kscale;
