@@ -346,6 +346,57 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_contract_through_diag(
     const long* labels_s, size_t ndim_s, const ndt_blocksparse_c64* b, const long* labels_b, size_t ndim_b, int rank,
     int nranks, int* status);
 
+/* ---- Multi-GPU: NCCL communicator and gathered block-sparse contractions
+ * (no counterpart in the reference, which is single-threaded CPU code; the
+ * per-output-block loop these distribute is contract/blocksparse.rs:144-180).
+ * One process per GPU.  Rank 0 calls ndt_b200_comm_unique_id and hands the
+ * 128 bytes to every rank by its own means (MPI, a TCP store, torch.distributed);
+ * each rank, with its GPU current, calls ndt_b200_comm_init.  A caller that
+ * already holds an ncclComm_t (for this process's current GPU) wraps it with
+ * ndt_b200_comm_from_nccl; it stays the caller's (release does not destroy it).
+ * NCCL is loaded at the first of these calls (libnccl.so.2; a copy already
+ * loaded in the process, e.g. torch's, is shared).  Release a communicator
+ * before its NCCL library's process teardown. */
+typedef struct ndt_comm ndt_comm;
+int ndt_b200_comm_unique_id(unsigned char* id /* 128 bytes out */);
+ndt_comm* ndt_b200_comm_init(const unsigned char* id, int nranks, int rank, int* status);
+ndt_comm* ndt_b200_comm_from_nccl(void* nccl_comm /* ncclComm_t */, int* status);
+int ndt_b200_comm_rank(const ndt_comm* comm);
+int ndt_b200_comm_size(const ndt_comm* comm);
+void ndt_b200_comm_release(ndt_comm* comm);
+
+/* contract_blocksparse with the output gathered on every rank (the contract
+ * "gather" flag; device list = the communicator's ranks).  Every rank passes
+ * the same operands; each computes its share of the output blocks (longest
+ * processing time on tile cost, as contract_shard) straight into their places
+ * in the packed, sorted output and receives the others' blocks there over
+ * NCCL point to point, chunk by chunk while it computes.  Every rank returns
+ * the unsharded result (same structure and values as
+ * ndt_blocksparse_*_contract).  Collective: every rank of the communicator
+ * must call it, with the same arguments. */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_gathered(const ndt_blocksparse_f64* a, const long* labels_a,
+                                                           size_t ndim_a, const ndt_blocksparse_f64* b,
+                                                           const long* labels_b, size_t ndim_b, ndt_comm* comm,
+                                                           int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_gathered(const ndt_blocksparse_c64* a, const long* labels_a,
+                                                           size_t ndim_a, const ndt_blocksparse_c64* b,
+                                                           const long* labels_b, size_t ndim_b, ndt_comm* comm,
+                                                           int* status);
+/* (A . S) . B (see contract_through_diag), gathered on every rank as above. */
+ndt_blocksparse_f64* ndt_blocksparse_f64_contract_through_diag_gathered(
+    const ndt_blocksparse_f64* a, const long* labels_a, size_t ndim_a, const ndt_diagblocksparse_f64* s,
+    const long* labels_s, size_t ndim_s, const ndt_blocksparse_f64* b, const long* labels_b, size_t ndim_b,
+    ndt_comm* comm, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_contract_through_diag_gathered(
+    const ndt_blocksparse_c64* a, const long* labels_a, size_t ndim_a, const ndt_diagblocksparse_c64* s,
+    const long* labels_s, size_t ndim_s, const ndt_blocksparse_c64* b, const long* labels_b, size_t ndim_b,
+    ndt_comm* comm, int* status);
+/* The whole output of a sharded contraction on every rank, from each rank's
+ * shard (contract_shard / contract_through_diag with rank, nranks = the
+ * communicator's).  Collective. */
+ndt_blocksparse_f64* ndt_blocksparse_f64_allgather(const ndt_blocksparse_f64* shard, ndt_comm* comm, int* status);
+ndt_blocksparse_c64* ndt_blocksparse_c64_allgather(const ndt_blocksparse_c64* shard, ndt_comm* comm, int* status);
+
 /* Dense f64 contraction that allocates no memory (no counterpart in the
  * reference).  For callers that may not call cudaMalloc -- allocation-free
  * hot loops, hosts that own the device memory budget, graph-oriented

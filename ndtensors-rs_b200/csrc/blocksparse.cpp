@@ -24,6 +24,7 @@
 #include <unordered_map>
 
 #include "../../include/ndtensors_capi.h"
+#include "ndt_comm.h"
 #include "ndt_internal.h"
 
 namespace ndt {
@@ -173,12 +174,31 @@ struct ThroughDiag {
   bool real = false;  // every diagonal value real (one multiply per component)
 };
 
+// Overlap of compute and gather in a gathered contraction: each rank's
+// output blocks (by descending tile cost) are dealt round-robin into this
+// many chunks; chunk c's transfers run while chunk c + 1 computes, on SMs
+// that chunk's launch leaves free.
+constexpr int kGatherChunks = 3;
+constexpr int kGatherSmReserve = 16;
+
 // `select` (nsel output coordinates of rank |ua| + |ub|, natural order):
 // compute only those output blocks (the ones the pairs produce), e.g. one
 // rank's share when its operands hold only the blocks that share references.
+// `gcomm` (gathered mode): rank and nranks are the communicator's; this rank
+// computes its share of the output blocks straight into their places in the
+// whole output, and every rank receives the other ranks' blocks there over
+// NCCL (point-to-point, no padding, no assembly copy), chunk by chunk behind
+// the compute.  The result is the unsharded tensor on every rank.
 BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
                          const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
-                         const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr) {
+                         const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr,
+                         Comm* gcomm = nullptr) {
+  if (gcomm) {
+    rank = comm_rank(*gcomm);
+    nranks = comm_size(*gcomm);
+    if (comm_device(*gcomm) != current_device())
+      throw Error(ErrKind::InvalidArgument, "the communicator belongs to another device than the current one");
+  }
   const size_t na = A.ndim(), nb = B.ndim();
   if (A.dt != B.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
   if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
@@ -325,9 +345,13 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     }
     return C;
   }
-  for (size_t i = 0; i < all_out.size(); i++)
-    if (owner[i] == rank) C.coords.push_back(all_out[i]);
-  if (nranks > 1) {
+  if (gcomm) {
+    C.coords = all_out;
+  } else {
+    for (size_t i = 0; i < all_out.size(); i++)
+      if (owner[i] == rank) C.coords.push_back(all_out[i]);
+  }
+  if (nranks > 1 && !gcomm) {
     auto lay = std::make_shared<ShardLayout>();
     lay->nranks = nranks;
     lay->coords = all_out;
@@ -394,37 +418,94 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     b_kmajor = true;
   }
   // device table: one problem per output block, one segment per pair
-  std::vector<GroupedProblem> probs;
-  std::vector<GroupedSegment> segs;
-  for (size_t ob = 0; ob < C.nnzb(); ob++) {
-    const auto& prs = contrib[C.coords[ob]];
-    GroupedProblem pr{};
-    int64_t m = 1, n = 1;
-    for (size_t i : ua) m *= (int64_t)A.bsz[i][A.coords[prs[0].first][i]];
-    for (size_t j : ub) n *= (int64_t)B.bsz[j][B.coords[prs[0].second][j]];
-    pr.m = m;
-    pr.n = n;
-    pr.c_off = (int64_t)C.offs[ob];
-    pr.seg_begin = (int64_t)segs.size();
-    pr.seg_count = (int64_t)prs.size();
-    for (auto& p2 : prs) {
-      GroupedSegment sg{};
-      int64_t k = 1;
-      for (size_t i : pa) k *= (int64_t)A.bsz[i][A.coords[p2.first][i]];
-      sg.a_off = (int64_t)A.offs[p2.first];
-      sg.b_off = (int64_t)B.offs[p2.second];
-      sg.k = k;
-      sg.lda = a_kmajor ? k : m;
-      sg.ldb = b_kmajor ? k : n;
-      sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
-      segs.push_back(sg);
+  auto make_table = [&](const std::vector<size_t>& obs, std::vector<GroupedProblem>& probs,
+                        std::vector<GroupedSegment>& segs) {
+    for (size_t ob : obs) {
+      const auto& prs = contrib[C.coords[ob]];
+      GroupedProblem pr{};
+      int64_t m = 1, n = 1;
+      for (size_t i : ua) m *= (int64_t)A.bsz[i][A.coords[prs[0].first][i]];
+      for (size_t j : ub) n *= (int64_t)B.bsz[j][B.coords[prs[0].second][j]];
+      pr.m = m;
+      pr.n = n;
+      pr.c_off = (int64_t)C.offs[ob];
+      pr.seg_begin = (int64_t)segs.size();
+      pr.seg_count = (int64_t)prs.size();
+      for (auto& p2 : prs) {
+        GroupedSegment sg{};
+        int64_t k = 1;
+        for (size_t i : pa) k *= (int64_t)A.bsz[i][A.coords[p2.first][i]];
+        sg.a_off = (int64_t)A.offs[p2.first];
+        sg.b_off = (int64_t)B.offs[p2.second];
+        sg.k = k;
+        sg.lda = a_kmajor ? k : m;
+        sg.ldb = b_kmajor ? k : n;
+        sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
+        segs.push_back(sg);
+      }
+      probs.push_back(pr);
     }
-    probs.push_back(pr);
-  }
+  };
   void* Cd = C.st->dev_overwrite();
   void* Cu = permute_c ? dev_alloc(C.total() * es, dev) : Cd;
-  grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, td_pos != SIZE_MAX ? td->sdata : nullptr, s,
-               td_pos != SIZE_MAX && td->real);
+  const void* kscale = td_pos != SIZE_MAX ? td->sdata : nullptr;
+  const bool kreal = td_pos != SIZE_MAX && td->real;
+  if (!gcomm) {
+    std::vector<size_t> obs(C.nnzb());
+    for (size_t i = 0; i < obs.size(); i++) obs[i] = i;
+    std::vector<GroupedProblem> probs;
+    std::vector<GroupedSegment> segs;
+    make_table(obs, probs, segs);
+    grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, kscale, s, kreal);
+  } else {
+    // Chunks: every rank's blocks by descending tile cost, dealt round-robin
+    // (every rank derives the same chunk of every block, so each transfer's
+    // sender and receiver issue it in the same group, in block order).
+    std::vector<int> chunk(all_out.size(), 0);
+    {
+      std::vector<size_t> order(all_out.size());
+      for (size_t i = 0; i < order.size(); i++) order[i] = i;
+      std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return cost[x] > cost[y]; });
+      std::vector<int> dealt(nranks, 0);
+      for (size_t i : order) chunk[i] = dealt[owner[i]]++ % kGatherChunks;
+    }
+    const size_t dpe = es / 8;  // doubles per element
+    Comm& cm = *gcomm;
+    for (int c = 0; c < kGatherChunks; c++) {
+      std::vector<size_t> mine;
+      for (size_t i = 0; i < all_out.size(); i++)
+        if (owner[i] == rank && chunk[i] == c) mine.push_back(i);
+      if (!mine.empty()) {
+        std::vector<GroupedProblem> probs;
+        std::vector<GroupedSegment> segs;
+        make_table(mine, probs, segs);
+        grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, kscale, s, kreal,
+                     nranks > 1 ? kGatherSmReserve : 0);
+      }
+      // this chunk's blocks: runs of consecutive blocks (contiguous in the
+      // packed output) with one owner; the owner sends, the others receive
+      std::vector<P2POp> ops;
+      for (size_t i = 0; i < all_out.size();) {
+        if (chunk[i] != c) {
+          i++;
+          continue;
+        }
+        size_t j = i + 1;
+        while (j < all_out.size() && chunk[j] == c && owner[j] == owner[i]) j++;
+        char* p = (char*)Cu + C.offs[i] * es;
+        const size_t nd = (C.offs[j] - C.offs[i]) * dpe;
+        if (owner[i] == rank) {
+          for (int q = 0; q < nranks; q++)
+            if (q != rank) ops.push_back(P2POp{true, q, p, nd});
+        } else {
+          ops.push_back(P2POp{false, owner[i], p, nd});
+        }
+        i = j;
+      }
+      comm_exchange(cm, ops, s, nullptr);
+    }
+    comm_join(cm, s);
+  }
   if (permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,
     // checked above); the data is permuted block by block.
@@ -698,7 +779,12 @@ BlockSparseT bs_contract_diag(const BlockSparseT& A, const std::vector<int32_t>&
 // the output blocks, as contract_shard assigns them.
 BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<int32_t>& la,
                                       const DiagBlockSparseT& S, const std::vector<int32_t>& ls,
-                                      const BlockSparseT& B, const std::vector<int32_t>& lb, int rank, int nranks) {
+                                      const BlockSparseT& B, const std::vector<int32_t>& lb, int rank, int nranks,
+                                      Comm* gcomm = nullptr) {
+  if (gcomm) {
+    rank = comm_rank(*gcomm);
+    nranks = comm_size(*gcomm);
+  }
   const BlockSparseT& t = S.s;
   if (la.size() != A.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
   if (lb.size() != B.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_b length != ndim(b)");
@@ -750,7 +836,7 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
   if (fused) {
     std::vector<int32_t> lb2(lb);
     lb2[ax_b] = x;  // pair A's axis with B's through the diagonal
-    return bs_contract(A, la, B, lb2, rank, nranks, nullptr, nullptr, 0, &td);
+    return bs_contract(A, la, B, lb2, rank, nranks, nullptr, nullptr, 0, &td, gcomm);
   }
   const int32_t P = pmax + 1;
   BlockSparseT AS = bs_contract_diag(A, la, S, {x, P});
@@ -759,7 +845,60 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
     if (u != x) las.push_back(u);
   std::sort(las.begin(), las.end());
   las.push_back(y);
-  return bs_contract(AS, las, B, lb, rank, nranks);
+  return bs_contract(AS, las, B, lb, rank, nranks, nullptr, nullptr, 0, nullptr, gcomm);
+}
+
+// The whole output of a sharded contraction on every rank, from this rank's
+// shard (which carries the layout: every output block and its owner).  The
+// rank's own blocks are copied to their places in the packed, sorted output;
+// the others arrive there over NCCL point to point, one transfer per run of
+// consecutive blocks with one owner (no padding, no assembly copy).
+BlockSparseT bs_allgather(const BlockSparseT& shard, Comm& cm) {
+  if (!shard.layout) throw Error(ErrKind::InvalidArgument, "allgather needs a shard of a sharded contraction");
+  const ShardLayout& L = *shard.layout;
+  const int rank = comm_rank(cm), nranks = comm_size(cm);
+  if (L.nranks != nranks) throw Error(ErrKind::InvalidArgument, "the shard was cut for another number of ranks");
+  if (comm_device(cm) != current_device())
+    throw Error(ErrKind::InvalidArgument, "the communicator belongs to another device than the current one");
+  std::vector<std::vector<size_t>> mine;
+  for (size_t i = 0; i < L.coords.size(); i++)
+    if (L.owner[i] == rank) mine.push_back(L.coords[i]);
+  if (mine != shard.coords) throw Error(ErrKind::InvalidArgument, "the shard does not belong to this rank");
+  BlockSparseT C = make_bs(shard.dt, shard.bsz, L.coords);
+  if (C.total() == 0) return C;
+  const size_t es = esize(C.dt);
+  cudaStream_t s = ctx().compute;
+  void* d = C.st->dev_overwrite();
+  if (shard.total()) {
+    const void* src = shard.st->dev_read();
+    std::vector<int64_t> so, dso, nb;
+    size_t r = 0;
+    for (size_t i = 0; i < L.coords.size(); i++)
+      if (L.owner[i] == rank) {
+        so.push_back((int64_t)(shard.offs[r] * es));
+        dso.push_back((int64_t)(C.offs[i] * es));
+        nb.push_back((int64_t)(shard.block_elems(shard.coords[r]) * es));
+        r++;
+      }
+    copy_segments(src, d, so, dso, nb, s);
+  }
+  std::vector<P2POp> ops;
+  const size_t dpe = es / 8;
+  for (size_t i = 0; i < L.coords.size();) {
+    size_t j = i + 1;
+    while (j < L.coords.size() && L.owner[j] == L.owner[i]) j++;
+    char* p = (char*)d + C.offs[i] * es;
+    const size_t n = (C.offs[j] - C.offs[i]) * dpe;
+    if (L.owner[i] == rank) {
+      for (int q = 0; q < nranks; q++)
+        if (q != rank) ops.push_back(P2POp{true, q, p, n});
+    } else {
+      ops.push_back(P2POp{false, L.owner[i], p, n});
+    }
+    i = j;
+  }
+  comm_exchange(cm, ops, s, s);
+  return C;
 }
 
 // A block-sparse tensor from blocks lying anywhere in device memory: block i
@@ -1221,5 +1360,45 @@ NDT_BS_FROM_DENSE(ndt_blocksparse_c64, ndt_tensor_c64, c64)
   }
 NDT_DIAG(ndt_diagblocksparse_f64, ndt_tensor_f64, ndt_blocksparse_f64, f64)
 NDT_DIAG(ndt_diagblocksparse_c64, ndt_tensor_c64, ndt_blocksparse_c64, c64)
+
+// Gathered multi-GPU contractions over an ndt_comm (comm.cpp).
+#define NDT_GATHER(TB, TD, DT)                                                                                          \
+  TB* ndt_blocksparse_##DT##_contract_gathered(const TB* a, const long* la, size_t na, const TB* b, const long* lb,   \
+                                               size_t nb, ndt_comm* comm, int* status) {                               \
+    if (!status) return nullptr;                                                                                        \
+    if (!a || !b || !comm || (!la && na) || (!lb && nb)) {                                                              \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                    \
+      return new NdtBs{bs_contract(((const NdtBs*)a)->t, labels(la, na), ((const NdtBs*)b)->t, labels(lb, nb), 0, 1,   \
+                                   nullptr, nullptr, 0, nullptr, &comm_of(comm))};                                      \
+    });                                                                                                                 \
+  }                                                                                                                     \
+  TB* ndt_blocksparse_##DT##_contract_through_diag_gathered(const TB* a, const long* la, size_t na, const TD* s,       \
+                                                            const long* ls, size_t ns, const TB* b, const long* lb,     \
+                                                            size_t nb, ndt_comm* comm, int* status) {                   \
+    if (!status) return nullptr;                                                                                        \
+    if (!a || !s || !b || !comm || (!la && na) || (!ls && ns) || (!lb && nb)) {                                         \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH, [&]() -> void* {                                                    \
+      return new NdtBs{bs_contract_through_diag(((const NdtBs*)a)->t, labels(la, na), ((const NdtDiag*)s)->t,           \
+                                                labels(ls, ns), ((const NdtBs*)b)->t, labels(lb, nb), 0, 1,             \
+                                                &comm_of(comm))};                                                       \
+    });                                                                                                                 \
+  }                                                                                                                     \
+  TB* ndt_blocksparse_##DT##_allgather(const TB* shard, ndt_comm* comm, int* status) {                                \
+    if (!status) return nullptr;                                                                                        \
+    if (!shard || !comm) {                                                                                              \
+      *status = NDT_INVALID_ARGUMENT;                                                                                   \
+      return nullptr;                                                                                                   \
+    }                                                                                                                   \
+    return (TB*)guarded(status, NDT_SHAPE_MISMATCH,                                                                     \
+                        [&]() -> void* { return new NdtBs{bs_allgather(((const NdtBs*)shard)->t, comm_of(comm))}; });  \
+  }
+NDT_GATHER(ndt_blocksparse_f64, ndt_diagblocksparse_f64, f64)
+NDT_GATHER(ndt_blocksparse_c64, ndt_diagblocksparse_c64, c64)
 
 }  // extern "C"

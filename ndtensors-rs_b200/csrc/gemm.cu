@@ -55,6 +55,7 @@ struct KArgs {
   int accumulate;
   int ntiles;          // grouped mode: entries of `tiles`
   int* counter;        // grouped mode: tile reservation counter (zero at launch)
+  int sm_reserve;      // grouped mode: SMs to leave free of persistent CTAs
 };
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
@@ -883,7 +884,8 @@ void launch_grouped(const KArgs& a, cudaStream_t s) {
   auto kern = dmma_grouped_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, SCALE>;
   ensure_dynamic_smem((const void*)kern, C::smem_bytes);
   const int per_sm = resident_per_sm((const void*)kern, C::kThreads, C::smem_bytes);
-  const int grid = (int)std::min<int64_t>(a.ntiles, (int64_t)per_sm * ctx().sm_count);
+  const int sms = std::max(1, ctx().sm_count - std::max(0, a.sm_reserve));
+  const int grid = (int)std::min<int64_t>(a.ntiles, (int64_t)per_sm * sms);
   launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
   count_launch();
   NDT_CUDA(cudaGetLastError());
@@ -1050,7 +1052,7 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
 
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* kscale, cudaStream_t s, bool kscale_real) {
+                  const void* kscale, cudaStream_t s, bool kscale_real, int sm_reserve) {
   if (probs.empty()) return;
   const bool cplx = dt == DType::C128;
   const DeviceCtx& c = ctx();
@@ -1126,6 +1128,7 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.C = Cp;
   a.tiles = (const int4*)(d + off_t);
   a.counter = (int*)(d + off_c);
+  a.sm_reserve = sm_reserve;
   a.probs = (const GroupedProblem*)d;
   a.segs = (const GroupedSegment*)(d + off_s);
   a.kscale = kscale;

@@ -256,9 +256,11 @@ struct GroupedSegment {
   int64_t lda, ldb;
   int64_t scale_off;     // offset into the k-scale vector, or -1
 };
+// sm_reserve: SMs left free of the launch's persistent CTAs (room for
+// transfer kernels that run beside it, e.g. NCCL's).
 void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* kscale, cudaStream_t s, bool kscale_real = false);
+                  const void* kscale, cudaStream_t s, bool kscale_real = false, int sm_reserve = 0);
 
 // Block-sparse device helpers (blocksparse_kernels.cu).  A block table entry
 // describes one block: its extents, and for the dense side its start offset

@@ -143,8 +143,20 @@ SIGNATURES = [
             (f"ndt_blocksparse_{dt}_contract_through_diag", vp,
              [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t,
               ctypes.c_int, ctypes.c_int, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_gathered", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, vp, c_int_p]),
+            (f"ndt_blocksparse_{dt}_contract_through_diag_gathered", vp,
+             [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, vp,
+              c_int_p]),
+            (f"ndt_blocksparse_{dt}_allgather", vp, [vp, vp, c_int_p]),
         ]
     ],
+    ("ndt_b200_comm_unique_id", ctypes.c_int, [ctypes.c_char_p]),
+    ("ndt_b200_comm_init", vp, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, c_int_p]),
+    ("ndt_b200_comm_from_nccl", vp, [vp, c_int_p]),
+    ("ndt_b200_comm_rank", ctypes.c_int, [vp]),
+    ("ndt_b200_comm_size", ctypes.c_int, [vp]),
+    ("ndt_b200_comm_release", None, [vp]),
     (
         "ndt_b200_contract_f64_noalloc",
         ctypes.c_int,

@@ -405,7 +405,92 @@ def _host_group(group, dist):
     return g
 
 
-def allgather(shard, group=None):
+class Comm:
+    """The library's NCCL communicator (ndt_comm) over the ranks of a job, one
+    process per GPU.  ``Comm.from_group(group)`` builds it collectively over a
+    torch.distributed group: rank 0 creates NCCL's unique id and the group
+    broadcasts it.  Used by contract_gathered, contract_through_diag_gathered
+    and allgather, which gather a sharded result in the library (NCCL point to
+    point, straight into the output's block offsets)."""
+
+    _by_group = {}
+
+    def __init__(self, ptr: int):
+        self._lib = get_lib()
+        self._ptr = ptr
+
+    def __del__(self):
+        if getattr(self, "_ptr", None):
+            self._lib.ndt_b200_comm_release(self._ptr)
+            self._ptr = None
+
+    release = __del__
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = ctypes.create_string_buffer(128)
+        check_status(get_lib().ndt_b200_comm_unique_id(buf), "comm_unique_id")
+        return buf.raw
+
+    @classmethod
+    def init(cls, uid: bytes, nranks: int, rank: int) -> "Comm":
+        st = ctypes.c_int(-999)
+        p = get_lib().ndt_b200_comm_init(uid, int(nranks), int(rank), ctypes.byref(st))
+        check_status(st.value, "comm_init")
+        return cls(p)
+
+    @classmethod
+    def from_group(cls, group=None) -> "Comm":
+        """Collective over `group` (default: the world); cached per group."""
+        import torch.distributed as dist
+
+        key = id(group) if group is not None else None
+        c = cls._by_group.get(key)
+        if c is None:
+            obj = [cls.unique_id() if dist.get_rank(group) == 0 else None]
+            src = dist.get_global_rank(group, 0) if group is not None else 0
+            dist.broadcast_object_list(obj, src=src, group=group)
+            c = cls._by_group[key] = cls.init(obj[0], dist.get_world_size(group), dist.get_rank(group))
+        return c
+
+    @property
+    def rank(self) -> int:
+        return int(self._lib.ndt_b200_comm_rank(self._ptr))
+
+    @property
+    def size(self) -> int:
+        return int(self._lib.ndt_b200_comm_size(self._ptr))
+
+
+def contract_gathered(a, labels_a, b, labels_b, comm: Comm):
+    """contract() with the work split over the communicator's ranks and the
+    result gathered on every rank (collective: every rank calls it with the
+    same operands).  Each rank computes its share of the output blocks into
+    their places in the output and receives the others' over NCCL while it
+    computes."""
+    la, na = _labels(labels_a)
+    lb, nb = _labels(labels_b)
+    st = ctypes.c_int(-999)
+    p = a._f("contract_gathered")(a._ptr, la, na, b._ptr, lb, nb, comm._ptr, ctypes.byref(st))
+    _raise(st.value, "blocksparse contract_gathered")
+    return type(a)(p)
+
+
+def contract_through_diag_gathered(a, labels_a, s, labels_s, b, labels_b, comm: Comm):
+    """contract_through_diag() split over the communicator's ranks (one
+    grouped launch per chunk with S applied as the operands load) and gathered
+    on every rank (collective)."""
+    la, na = _labels(labels_a)
+    ls, ns = _labels(labels_s)
+    lb, nb = _labels(labels_b)
+    st = ctypes.c_int(-999)
+    p = a._f("contract_through_diag_gathered")(a._ptr, la, na, s._ptr, ls, ns, b._ptr, lb, nb, comm._ptr,
+                                                 ctypes.byref(st))
+    _raise(st.value, "blocksparse contract_through_diag_gathered")
+    return type(a)(p)
+
+
+def allgather(shard, group=None, comm: Comm = None):
     """Gather every rank's shard (disjoint output blocks of one contraction)
     into the full block-sparse tensor on all ranks, with torch.distributed.
     Blocks come out sorted, as contract_blocksparse orders them.
@@ -421,10 +506,24 @@ def allgather(shard, group=None):
     NVLink, and the library assembles the sorted tensor from the gathered
     buffer with one copy kernel (from_device_blocks).  Nothing on the host
     waits for the device.  On gloo (CPU tests) the same steps run on host
-    tensors."""
+    tensors.
+
+    With `comm` (or on an NCCL group, for a shard that carries its layout)
+    the library gathers the shard itself: NCCL point-to-point transfers
+    straight into the output's block offsets, no padding and no assembly
+    copy (ndt_blocksparse_*_allgather)."""
     import torch
     import torch.distributed as dist
 
+    layout0 = shard._shard_layout()
+    if comm is None and layout0 is not None and dist.get_backend(group) == "nccl" and \
+            layout0[0] == dist.get_world_size(group):
+        comm = Comm.from_group(group)
+    if comm is not None:
+        st = ctypes.c_int(-999)
+        p = shard._f("allgather")(shard._ptr, comm._ptr, ctypes.byref(st))
+        _raise(st.value, "blocksparse allgather")
+        return type(shard)(p)
     world = dist.get_world_size(group)
     nccl = dist.get_backend(group) == "nccl"
     dev = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")

@@ -2,10 +2,14 @@
 
 Each rank computes its cost-balanced share of the output blocks
 (contract_shard, contract_through_diag) and the shards are gathered in HBM
-(allgather: one NCCL all_gather of every rank's blocks, put in sorted order
-by one device concatenation).  The gathered tensor must
-equal the unsharded contraction on one GPU.  Runs as two spawned processes,
-one per GPU; skipped when fewer than two devices are visible.
+by the library (allgather over the library's NCCL communicator: point-to-point
+transfers straight into the output's block offsets).  The gathered
+contractions of the C ABI (contract_gathered, contract_through_diag_gathered:
+compute and gather chunk by chunk) are checked the same way, and the c128
+chain at bond 8192 block by block against the CPU block reference.  The
+gathered tensor must equal the unsharded contraction on one GPU (relative
+error 1e-12).  Runs as two spawned processes, one per GPU; skipped when fewer
+than two devices are visible.
 """
 
 from __future__ import annotations
@@ -64,6 +68,44 @@ def _worker(rank, world, port, q):
         ok = gathered.coords == full.coords and np.allclose(
             gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
         results.append(("cfg5 bond 1024 c128 through diag", bool(ok), -1, full.nnzblocks))
+        # the library's communicator and gathered contractions (C ABI)
+        comm = bs.Comm.from_group()
+        assert (comm.rank, comm.size) == (rank, world)
+        gathered = bs.allgather(bs.contract_through_diag(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], rank, world),
+                                comm=comm)
+        ok = gathered.coords == full.coords and np.allclose(
+            gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
+        results.append(("cfg5 bond 1024 allgather (library)", bool(ok), -1, full.nnzblocks))
+        gathered = bs.contract_through_diag_gathered(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], comm)
+        ok = gathered.coords == full.coords and np.allclose(
+            gathered.to_numpy_data(), full.to_numpy_data(), rtol=1e-12, atol=1e-12)
+        results.append(("cfg5 bond 1024 contract_through_diag_gathered", bool(ok), -1, full.nnzblocks))
+        (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=8)
+        A4 = bs.BlockSparseF64.from_blocks(sa, ca, a)
+        B4 = bs.BlockSparseF64.from_blocks(sb, cb, b)
+        full4 = bs.contract(A4, la, B4, lb)
+        g4 = bs.contract_gathered(A4, la, B4, lb, comm)
+        ok = g4.coords == full4.coords and np.array_equal(g4.to_numpy_data(), full4.to_numpy_data())
+        results.append(("cfg4/8 f64 contract_gathered (bit-exact)", bool(ok), -1, full4.nnzblocks))
+        # bond 8192 (the benchmark's size), every block against the CPU reference
+        from blockref import reference_blocks, rel_fro
+
+        Ah, Sh, Bh = cfg5_tensors()
+        A8 = bs.BlockSparseC64.from_blocks(*Ah)
+        S8 = bs.DiagBlockSparseC64.from_blocks(*Sh)
+        B8 = bs.BlockSparseC64.from_blocks(*Bh)
+        for _ in range(2):  # twice in a row: the second call reuses the communicator
+            g8 = bs.contract_through_diag_gathered(A8, [1, 2, -1], S8, [-1, -2], B8, [-2, 3, 4], comm)
+        _, c8, o8 = g8._structure()
+        d8 = g8.to_numpy_data()
+        ends = list(o8[1:]) + [len(d8)]
+        got = {tuple(int(x) for x in c): d8[o:e] for c, o, e in zip(c8, o8, ends)}
+        ref = reference_blocks(Ah, Bh, 2, 1, list(got), kscale=np.asarray(Sh[2]))
+        err = max(rel_fro(got[c], ref[c]) for c in ref)
+        results.append((f"cfg5 bond 8192 gathered vs CPU reference (max block err {err:.1e})",
+                        bool(err <= 1e-12 and len(got) == 128), -1, 128))
+        del comm
+        bs.Comm._by_group.clear()
         q.put((rank, results, None))
     except Exception as e:  # reported to the parent, which fails the test
         q.put((rank, results, repr(e)))
