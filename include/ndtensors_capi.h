@@ -134,6 +134,22 @@ ndt_tensor_c64* ndt_tensor_c64_contract_gemm(const ndt_tensor_c64* a, const long
                                              const ndt_tensor_c64* b, const long* labels_b, size_t ndim_b,
                                              int* status);
 
+/* contract_gemm split along one free index for multi-GPU use (no counterpart
+ * in the reference; the contraction split is gemm.rs:173-236).  The free axis
+ * labelled axis_label (a positive label of exactly one axis of A or B) is cut
+ * into nranks near-equal ranges; the call returns this rank's slab of C
+ * (range [N*rank/nranks, N*(rank+1)/nranks) of that axis, other axes whole,
+ * label-sorted as contract_gemm), reading the operand in place.  No
+ * collective: the slabs of all ranks together are contract_gemm's result.
+ * An empty range gives a zero tensor of the slab's shape.  Bad rank / nranks
+ * or label: NDT_INVALID_ARGUMENT; contraction errors as contract_gemm. */
+ndt_tensor_f64* ndt_tensor_f64_contract_gemm_shard(const ndt_tensor_f64* a, const long* labels_a, size_t ndim_a,
+                                                   const ndt_tensor_f64* b, const long* labels_b, size_t ndim_b,
+                                                   long axis_label, int rank, int nranks, int* status);
+ndt_tensor_c64* ndt_tensor_c64_contract_gemm_shard(const ndt_tensor_c64* a, const long* labels_a, size_t ndim_a,
+                                                   const ndt_tensor_c64* b, const long* labels_b, size_t ndim_b,
+                                                   long axis_label, int rank, int nranks, int* status);
+
 /* Device-pointer interop (the device-pointer ABI proposed in the reference's
  * README, "CUDA support" section).  from_device_ptr copies `len` elements from
  * device memory of the current device (the caller's writes to it must be

@@ -303,6 +303,30 @@ void* contract_impl(const void* a, const long* la, size_t na, const void* b, con
   return nullptr;
 }
 
+void* contract_shard_impl(const void* a, const long* la, size_t na, const void* b, const long* lb, size_t nb,
+                          long axis_label, int rank, int nranks, int* status) {
+  if (!status) return nullptr;
+  if (!a || !b || (!la && na) || (!lb && nb) || nranks < 1 || rank < 0 || rank >= nranks) {
+    set_last_error("contract_gemm_shard: NULL argument or rank outside [0, nranks)");
+    *status = NDT_INVALID_ARGUMENT;
+    return nullptr;
+  }
+  try {
+    NdtHandle* h = new NdtHandle{contract_gemm_shard(H(a)->t, labels_of(la, na), H(b)->t, labels_of(lb, nb),
+                                                     (int32_t)axis_label, rank, nranks)};
+    *status = NDT_SUCCESS;
+    return h;
+  } catch (const Error& e) {
+    *status = map_error(e, NDT_SHAPE_MISMATCH);
+  } catch (const std::exception& e) {
+    set_last_error(e.what());
+    *status = NDT_INTERNAL_ERROR;
+  } catch (...) {
+    *status = NDT_INTERNAL_ERROR;
+  }
+  return nullptr;
+}
+
 const double* device_ptr_impl(const void* t) {
   if (!t) return nullptr;
   try {
@@ -386,6 +410,11 @@ ndt_tensor_f64* ndt_tensor_f64_contract(const ndt_tensor_f64* a, const long* la,
 ndt_tensor_f64* ndt_tensor_f64_contract_gemm(const ndt_tensor_f64* a, const long* la, size_t na,
                                              const ndt_tensor_f64* b, const long* lb, size_t nb, int* status) {
   return (ndt_tensor_f64*)contract_impl(a, la, na, b, lb, nb, status, ContractSemantics::Gemm);
+}
+ndt_tensor_f64* ndt_tensor_f64_contract_gemm_shard(const ndt_tensor_f64* a, const long* la, size_t na,
+                                                   const ndt_tensor_f64* b, const long* lb, size_t nb, long axis_label,
+                                                   int rank, int nranks, int* status) {
+  return (ndt_tensor_f64*)contract_shard_impl(a, la, na, b, lb, nb, axis_label, rank, nranks, status);
 }
 
 void ndt_tensor_f64_contract_vjp(const ndt_tensor_f64* a, const long* la, size_t na, const ndt_tensor_f64* b,
@@ -518,6 +547,11 @@ ndt_tensor_c64* ndt_tensor_c64_contract(const ndt_tensor_c64* a, const long* la,
 ndt_tensor_c64* ndt_tensor_c64_contract_gemm(const ndt_tensor_c64* a, const long* la, size_t na,
                                              const ndt_tensor_c64* b, const long* lb, size_t nb, int* status) {
   return (ndt_tensor_c64*)contract_impl(a, la, na, b, lb, nb, status, ContractSemantics::Gemm);
+}
+ndt_tensor_c64* ndt_tensor_c64_contract_gemm_shard(const ndt_tensor_c64* a, const long* la, size_t na,
+                                                   const ndt_tensor_c64* b, const long* lb, size_t nb, long axis_label,
+                                                   int rank, int nranks, int* status) {
+  return (ndt_tensor_c64*)contract_shard_impl(a, la, na, b, lb, nb, axis_label, rank, nranks, status);
 }
 
 // ------------------------------------------------------- device interop

@@ -228,8 +228,16 @@ static void validate_perm_like_permutedims(const std::vector<size_t>& perm, size
   }
 }
 
+// A sub-range [lo, hi) of one free axis of one operand (0: A, 1: B): the
+// contraction then produces the matching slab of C.  The operand is read in
+// place through its own strides (base moved by lo along the axis).
+struct Slab {
+  int operand;
+  size_t axis, lo, hi;
+};
+
 static Dense contract_gemm_sem(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
-                               const std::vector<int32_t>& lb) {
+                               const std::vector<int32_t>& lb, const Slab* slab = nullptr) {
   const size_t na = a.ndim(), nb = b.ndim();
   // gemm.rs:54-79
   if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
@@ -294,10 +302,22 @@ static Dense contract_gemm_sem(const Dense& a, const std::vector<int32_t>& la, c
     if (olab[perm_c[i]] != olab[i]) permute_c = true;
 
   std::vector<size_t> sa = col_major_strides(a.shape), sb = col_major_strides(b.shape);
+  // the operands' extents as read (a slab narrows one free axis) and the
+  // element offset of each operand's first element read
+  std::vector<size_t> ash(a.shape), bsh(b.shape);
+  size_t a0 = 0, b0 = 0, alen = a.len(), blen = b.len();
+  if (slab) {
+    std::vector<size_t>& sh = slab->operand == 0 ? ash : bsh;
+    sh[slab->axis] = slab->hi - slab->lo;
+    (slab->operand == 0 ? a0 : b0) = slab->lo * (slab->operand == 0 ? sa : sb)[slab->axis];
+    (slab->operand == 0 ? alen : blen) = prod_max1(sh);
+    for (size_t i = 0; i < ua.size(); i++) oshape[i] = ash[ua[i]];
+    for (size_t j = 0; j < ub.size(); j++) oshape[ua.size() + j] = bsh[ub[j]];
+  }
   std::vector<Ax1> M, N;
   std::vector<AxK> K;
-  for (size_t i : ua) M.push_back({(int64_t)a.shape[i], (int64_t)sa[i]});
-  for (size_t j : ub) N.push_back({(int64_t)b.shape[j], (int64_t)sb[j]});
+  for (size_t i : ua) M.push_back({(int64_t)ash[i], (int64_t)sa[i]});
+  for (size_t j : ub) N.push_back({(int64_t)bsh[j], (int64_t)sb[j]});
   for (size_t p = 0; p < pa_.size(); p++)
     K.push_back({(int64_t)a.shape[pa_[p]], (int64_t)sa[pa_[p]], (int64_t)sb[pb_[p]]});
   size_t m = std::max<size_t>(1, prod(std::vector<size_t>(oshape.begin(), oshape.begin() + ua.size())));
@@ -305,25 +325,80 @@ static Dense contract_gemm_sem(const Dense& a, const std::vector<int32_t>& la, c
   size_t kk = 1;
   for (size_t p : pa_) kk *= a.shape[p];
   kk = std::max<size_t>(kk, 1);
+  const size_t es = esize(a.dt);
+  const void* ap = (const char*)a.st->dev_read() + a0 * es;
+  const void* bp = (const char*)b.st->dev_read() + b0 * es;
   if (full) {
     // contract_full (gemm.rs:98-125): dot product -> shape [1]
     Dense out = make_empty_device(a.dt, {1});
-    strided_contract(a.dt, a.st->dev_read(), b.st->dev_read(), out.st->dev, {}, {}, K, ctx().compute);
+    strided_contract(a.dt, ap, bp, out.st->dev, {}, {}, K, ctx().compute);
     return out;
   }
   // as_faer_mat asserts rows*cols == len (faer_interop.rs:72-84)
   if (outer) {
-    if (m != a.len() || n != b.len()) throw Error(ErrKind::Panic, "matrix view size mismatch");
+    if (m != alen || n != blen) throw Error(ErrKind::Panic, "matrix view size mismatch");
   } else {
-    if (m * kk != a.len() || kk * n != b.len()) throw Error(ErrKind::Panic, "matrix view size mismatch");
+    if (m * kk != alen || kk * n != blen) throw Error(ErrKind::Panic, "matrix view size mismatch");
   }
   std::vector<size_t> shape_unsorted = oshape;
   if (shape_unsorted.empty()) shape_unsorted.push_back(1);
   if (m * n != prod_max1(shape_unsorted)) throw Error(ErrKind::ShapeMismatch, "output length mismatch");
   Dense c = make_empty_device(a.dt, shape_unsorted);
-  strided_contract(a.dt, a.st->dev_read(), b.st->dev_read(), c.st->dev, M, N, K, ctx().compute);
+  strided_contract(a.dt, ap, bp, c.st->dev, M, N, K, ctx().compute);
   if (!permute_c) return c;
   return permutedims(c, perm_c);
+}
+
+// contract_gemm split along a free index (the dense multi-GPU scheme: no
+// reduction, each rank owns a slab of C).  The free axis labelled
+// `axis_label` (in A or in B, once) is cut into nranks near-equal ranges;
+// rank r contracts its range [N r / nranks, N (r + 1) / nranks) and returns
+// that slab of C (same label order as contract_gemm's result, the split axis
+// narrowed).  A rank whose range is empty gets a zero tensor of the slab's
+// shape.
+Dense contract_gemm_shard(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
+                          const std::vector<int32_t>& lb, int32_t axis_label, int rank, int nranks) {
+  if (a.dt != b.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
+  if (nranks < 1 || rank < 0 || rank >= nranks) throw Error(ErrKind::InvalidArgument, "need 0 <= rank < nranks");
+  if (axis_label <= 0) throw Error(ErrKind::InvalidArgument, "the split label must be a positive (free) label");
+  if (la.size() != a.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
+  if (lb.size() != b.ndim()) throw Error(ErrKind::WrongNumberOfIndices, "labels_b length != ndim(b)");
+  Slab sl{-1, 0, 0, 0};
+  int hits = 0;
+  for (size_t i = 0; i < la.size(); i++)
+    if (la[i] == axis_label) sl = Slab{0, i, 0, 0}, hits++;
+  for (size_t j = 0; j < lb.size(); j++)
+    if (lb[j] == axis_label) sl = Slab{1, j, 0, 0}, hits++;
+  if (hits != 1) throw Error(ErrKind::InvalidArgument, "the split label must label exactly one axis of A or B");
+  const size_t ext = (sl.operand == 0 ? a.shape : b.shape)[sl.axis];
+  sl.lo = ext * (size_t)rank / (size_t)nranks;
+  sl.hi = ext * (size_t)(rank + 1) / (size_t)nranks;
+  if (sl.hi == sl.lo) {
+    // An empty range: a zero tensor of the slab's shape.  Output axes as
+    // contract_gemm orders them (properties.rs:100-186): the unpaired axes
+    // of A, then of B, stably sorted by label.
+    std::vector<char> paired_a(la.size(), 0), paired_b(lb.size(), 0);
+    for (size_t i = 0; i < la.size(); i++) {
+      if (la[i] >= 0) continue;
+      for (size_t j = 0; j < lb.size(); j++)
+        if (la[i] == lb[j]) {
+          paired_a[i] = 1;
+          paired_b[j] = 1;
+          break;
+        }
+    }
+    std::vector<std::pair<int32_t, size_t>> out;  // (label, extent)
+    for (size_t i = 0; i < la.size(); i++)
+      if (!paired_a[i]) out.push_back({la[i], a.shape[i]});
+    for (size_t j = 0; j < lb.size(); j++)
+      if (!paired_b[j]) out.push_back({lb[j], b.shape[j]});
+    std::stable_sort(out.begin(), out.end(), [](const auto& x, const auto& y) { return x.first < y.first; });
+    std::vector<size_t> shape;
+    for (auto& o : out) shape.push_back(o.first == axis_label ? 0 : o.second);
+    if (shape.empty()) shape.push_back(1);
+    return make_uniform(a.dt, shape, 0.0, 0.0);
+  }
+  return contract_gemm_sem(a, la, b, lb, &sl);
 }
 
 Dense contract(const Dense& a, const std::vector<int32_t>& la, const Dense& b, const std::vector<int32_t>& lb,

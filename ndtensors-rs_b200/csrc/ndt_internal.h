@@ -294,6 +294,10 @@ void splitk_reduce(DType dt, const void* w, int nsplit, int64_t m, int64_t n, vo
 
 // Contractions
 enum class ContractSemantics { Naive, Gemm };
+// contract_gemm on the rank's range of the free axis labelled axis_label
+// (near-equal ranges over nranks): that slab of C (contract.cpp).
+Dense contract_gemm_shard(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
+                          const std::vector<int32_t>& lb, int32_t axis_label, int rank, int nranks);
 Dense contract(const Dense& a, const std::vector<int32_t>& la, const Dense& b,
                const std::vector<int32_t>& lb, ContractSemantics sem);
 void contract_vjp(const Dense& a, const std::vector<int32_t>& la, const Dense& b,

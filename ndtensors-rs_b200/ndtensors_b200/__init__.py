@@ -9,7 +9,7 @@ block-sparse tensors and whole-network contraction (contract_network).
 from . import blocksparse
 from ._lib import get_lib, last_error, lib_path
 from .network import contract_network
-from .ops import contract, contract_gemm, contract_jvp, contract_vjp
+from .ops import contract, contract_gemm, contract_gemm_shard, contract_jvp, contract_vjp
 from .tensor import NDTensorsError, StatusCode, TensorC64, TensorF64, check_status
 
 
@@ -49,6 +49,7 @@ __all__ = [
     "TensorC64",
     "contract",
     "contract_gemm",
+    "contract_gemm_shard",
     "contract_vjp",
     "contract_jvp",
     "contract_network",

@@ -151,6 +151,9 @@ SIGNATURES = [
             (f"ndt_blocksparse_{dt}_allgather", vp, [vp, vp, c_int_p]),
         ]
     ],
+    *[(f"ndt_tensor_{dt}_contract_gemm_shard", vp,
+       [vp, c_long_p, ctypes.c_size_t, vp, c_long_p, ctypes.c_size_t, ctypes.c_long, ctypes.c_int, ctypes.c_int,
+        c_int_p]) for dt in ("f64", "c64")],
     ("ndt_b200_comm_unique_id", ctypes.c_int, [ctypes.c_char_p]),
     ("ndt_b200_comm_init", vp, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, c_int_p]),
     ("ndt_b200_comm_from_nccl", vp, [vp, c_int_p]),

@@ -47,6 +47,24 @@ def contract_gemm(a, labels_a: Sequence[int], b, labels_b: Sequence[int]):
     return _contract("contract_gemm", a, labels_a, b, labels_b)
 
 
+def contract_gemm_shard(a, labels_a: Sequence[int], b, labels_b: Sequence[int], axis_label: int, rank: int,
+                        nranks: int):
+    """This rank's slab of contract_gemm(a, labels_a, b, labels_b), split
+    along the free axis labelled `axis_label` into `nranks` near-equal ranges
+    (no collective: the slabs of all ranks are the whole result)."""
+    if type(a) is not type(b):
+        raise TypeError("operands must have the same element type")
+    la, na = _labels(labels_a)
+    lb, nb = _labels(labels_b)
+    status = ctypes.c_int(-999)
+    ptr = getattr(get_lib(), f"ndt_tensor_{a._prefix}_contract_gemm_shard")(
+        a._ptr, la, na, b._ptr, lb, nb, int(axis_label), int(rank), int(nranks), ctypes.byref(status))
+    if status.value == StatusCode.SHAPE_MISMATCH:
+        raise ValueError("Contracted dimensions must have matching sizes")
+    check_status(status.value, "contract_gemm_shard")
+    return type(a)(ptr)
+
+
 def contract_vjp(a: TensorF64, labels_a: Sequence[int], b: TensorF64, labels_b: Sequence[int],
                  grad_output: TensorF64) -> Tuple[TensorF64, TensorF64]:
     la, na = _labels(labels_a)
