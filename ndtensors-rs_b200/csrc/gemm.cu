@@ -32,6 +32,7 @@
 #include <mutex>
 #include <queue>
 #include <type_traits>
+#include <unordered_map>
 #include <vector>
 
 #include "ndt_internal.h"
@@ -54,7 +55,7 @@ struct KArgs {
   int kscale_real;     // complex scale values whose imaginary parts are all zero
   int accumulate;
   int ntiles;          // grouped mode: entries of `tiles`
-  int* counter;        // grouped mode: tile reservation counter (zero at launch)
+  int* counter;        // grouped mode: [tiles reserved, CTAs done], zero at launch
   int sm_reserve;      // grouped mode: SMs to leave free of persistent CTAs
 };
 
@@ -856,6 +857,17 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     }
   }
   cp_wait<0>();
+  // The last CTA to finish leaves the reservation counters at zero for the
+  // next launch over the same table: every other CTA made its last
+  // reservation before it counted itself done.
+  if (tid == 0) {
+    __threadfence();
+    if (atomicAdd(args.counter + 1, 1) == G - 1) {
+      args.counter[0] = 0;
+      args.counter[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED,
@@ -1058,6 +1070,66 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
     dispatch<false>(a, grid, cls, A.kmajor, B.kmajor, vec, s);
 }
 
+namespace {
+
+struct PlanKey {
+  int device = -1;
+  int flags = 0;
+  std::vector<int64_t> words;  // the problems and segments, verbatim
+  bool operator==(const PlanKey& o) const { return device == o.device && flags == o.flags && words == o.words; }
+};
+struct PlanKeyHash {
+  size_t operator()(const PlanKey& k) const {
+    uint64_t h = 1469598103934665603ULL ^ (uint64_t)(k.device * 31 + k.flags);
+    for (int64_t w : k.words) h = (h ^ (uint64_t)w) * 1099511628211ULL;
+    return (size_t)h;
+  }
+};
+struct GroupedPlan {
+  char* d = nullptr;  // device table
+  size_t off_s = 0, off_t = 0, off_c = 0;
+  int cls = 0, ntiles = 0;
+  cudaEvent_t last_use = nullptr;  // the last launch that read the table
+  uint64_t tick = 0;
+};
+constexpr size_t kPlanCacheSize = 64;
+std::mutex g_plan_mu;
+std::unordered_map<PlanKey, GroupedPlan, PlanKeyHash> g_plans;
+uint64_t g_plan_tick = 0;
+
+const GroupedPlan* plan_lookup(const PlanKey& k) {
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  auto it = g_plans.find(k);
+  if (it == g_plans.end()) return nullptr;
+  it->second.tick = ++g_plan_tick;
+  return &it->second;
+}
+
+// Insert a plan, evicting the least recently used one of a full cache (its
+// table is freed once the last launch that read it has completed).
+const GroupedPlan* plan_insert(PlanKey&& k, const GroupedPlan& p) {
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  if (g_plans.size() >= kPlanCacheSize) {
+    auto victim = g_plans.begin();
+    for (auto it = g_plans.begin(); it != g_plans.end(); ++it)
+      if (it->second.tick < victim->second.tick) victim = it;
+    GroupedPlan& v = victim->second;
+    int prev = 0;
+    cudaGetDevice(&prev);
+    cudaSetDevice(victim->first.device);
+    cudaEventSynchronize(v.last_use);
+    cudaEventDestroy(v.last_use);
+    cudaFree(v.d);
+    cudaSetDevice(prev);
+    g_plans.erase(victim);
+  }
+  auto r = g_plans.emplace(std::move(k), p);
+  r.first->second.tick = ++g_plan_tick;
+  return &r.first->second;
+}
+
+}  // namespace
+
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
                   const void* kscale, cudaStream_t s, bool kscale_real, int sm_reserve) {
@@ -1105,45 +1177,69 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
     // per_sm - 1 others, at the class's relative rate
     *time = span * ((double)bm * bn * bk * tc.per_sm / tc.rate);
   };
-  std::vector<int4> tiles, cand;
-  int cls = 0;
-  double best = -1;
-  for (int cl = 0; cl < nclasses(cplx); cl++) {
-    double t;
-    build(cl, cand, &t);
-    if (best < 0 || t < best) {
-      best = t;
-      cls = cl;
-      tiles.swap(cand);
+  // The plan of a table (tile class, tile order, device copy of the table)
+  // depends only on the problems and segments: it is kept per device and
+  // reused by later calls with the same table (repeated contractions of one
+  // block structure), which then cost one launch and no host planning.
+  PlanKey key;
+  key.device = c.device;
+  key.flags = (cplx ? 1 : 0);
+  key.words.resize((probs.size() * sizeof(GroupedProblem) + segs.size() * sizeof(GroupedSegment)) / 8 + 1);
+  key.words[0] = (int64_t)probs.size();
+  memcpy(key.words.data() + 1, probs.data(), probs.size() * sizeof(GroupedProblem));
+  memcpy((char*)(key.words.data() + 1) + probs.size() * sizeof(GroupedProblem), segs.data(),
+         segs.size() * sizeof(GroupedSegment));
+  const GroupedPlan* plan = plan_lookup(key);
+  if (!plan) {
+    std::vector<int4> tiles, cand;
+    int cls = 0;
+    double best = -1;
+    for (int cl = 0; cl < nclasses(cplx); cl++) {
+      double t;
+      build(cl, cand, &t);
+      if (best < 0 || t < best) {
+        best = t;
+        cls = cl;
+        tiles.swap(cand);
+      }
     }
+    // Device-side tables: problems, segments, tiles, and the tile reservation
+    // counters (zero; each launch leaves them zero for the next), one allocation.
+    size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment),
+           bt = tiles.size() * sizeof(int4);
+    GroupedPlan np;
+    np.off_s = (bp + 255) / 256 * 256;
+    np.off_t = np.off_s + (bsg + 255) / 256 * 256;
+    np.off_c = np.off_t + (bt + 255) / 256 * 256;
+    const size_t total = np.off_c + 2 * sizeof(int);
+    std::vector<char> host(total);
+    memcpy(host.data(), probs.data(), bp);
+    memcpy(host.data() + np.off_s, segs.data(), bsg);
+    memcpy(host.data() + np.off_t, tiles.data(), bt);
+    np.d = (char*)pool_alloc(total, s);
+    NDT_CUDA(cudaMemcpyAsync(np.d, host.data(), total, cudaMemcpyHostToDevice, s));
+    // the copy reads pageable memory: it has been taken when the call returns
+    np.cls = cls;
+    np.ntiles = (int)tiles.size();
+    NDT_CUDA(cudaEventCreateWithFlags(&np.last_use, cudaEventDisableTiming));
+    plan = plan_insert(std::move(key), np);
   }
-  // Device-side tables: problems, segments, tiles (one allocation).
-  size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment),
-         bt = tiles.size() * sizeof(int4);
-  size_t off_s = (bp + 255) / 256 * 256, off_t = off_s + (bsg + 255) / 256 * 256;
-  size_t off_c = off_t + (bt + 255) / 256 * 256;  // tile reservation counter, uploaded as zero
-  size_t total = off_c + sizeof(int);
-  std::vector<char> host(total);
-  memcpy(host.data(), probs.data(), bp);
-  memcpy(host.data() + off_s, segs.data(), bsg);
-  memcpy(host.data() + off_t, tiles.data(), bt);
-  char* d = nullptr;
-  d = (char*)pool_alloc(total, s);
-  NDT_CUDA(cudaMemcpyAsync(d, host.data(), total, cudaMemcpyHostToDevice, s));
+  char* d = plan->d;
+  const int cls = plan->cls;
   KArgs a{};
   a.A = A;
   a.B = B;
   a.C = Cp;
-  a.tiles = (const int4*)(d + off_t);
-  a.counter = (int*)(d + off_c);
+  a.tiles = (const int4*)(d + plan->off_t);
+  a.counter = (int*)(d + plan->off_c);
   a.sm_reserve = sm_reserve;
   a.probs = (const GroupedProblem*)d;
-  a.segs = (const GroupedSegment*)(d + off_s);
+  a.segs = (const GroupedSegment*)(d + plan->off_s);
   a.kscale = kscale;
   a.kscale_real = kscale_real ? 1 : 0;
   a.accumulate = 0;
-  a.ntiles = (int)tiles.size();
-  int grid = (int)tiles.size();
+  a.ntiles = plan->ntiles;
+  int grid = plan->ntiles;
   bool vec = aligned16(A) && aligned16(B);
   for (const GroupedSegment& sg : segs)
     vec = vec && sg.a_off % 2 == 0 && sg.b_off % 2 == 0 && sg.lda % 2 == 0 && sg.ldb % 2 == 0;
@@ -1151,7 +1247,7 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
     dispatch<true>(a, grid, cls, a_kmajor, b_kmajor, false, s);
   else
     dispatch<false>(a, grid, cls, a_kmajor, b_kmajor, vec, s);
-  NDT_CUDA(cudaFreeAsync(d, s));
+  NDT_CUDA(cudaEventRecord(plan->last_use, s));
 }
 
 }  // namespace ndt
