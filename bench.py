@@ -746,6 +746,7 @@ def main():
         }
         print(json.dumps(line), flush=True)
     if pg:
+        ndt.blocksparse.Comm._by_group.clear()  # the library's communicators, before the group goes
         pg.barrier()
         pg.destroy_process_group()
     if not parity_ok:
@@ -899,14 +900,17 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     out.append(entry)
     del r5
     if world > 1:
-        msg, rg = timed(lambda: bs.allgather(chain()), 5)
+        comm = bs.Comm.from_group()
+        msg, rg = timed(lambda: bs.contract_through_diag_gathered(A, [1, 2, -1], S, [-1, -2], B, [-2, 3, 4], comm),
+                        5)
         # the gathered tensor: the unsharded block list, every block checked
         parg = block_parity(torch, bs, rg, Ah, Bh, 2, 1, world, kscale=np.asarray(sd), cplx=True, every=1,
                             expect_coords=all5)
         out.append({"cfg": "c5 c128 MPS+gather", "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "ms": msg, "n_gpus": world, "scaling": "strong", "parity": parg,
-                    "gather": "allgather (NCCL) of all output blocks to every rank",
-                    "workload": "block-sparse c128 two-site MPS, sharded + NCCL allgather of the output"})
+                    "gather": "gathered in the library (ndt_blocksparse_c64_contract_through_diag_gathered): "
+                              "NCCL point to point into the output's block offsets, chunked behind the compute",
+                    "workload": "block-sparse c128 two-site MPS, sharded + gathered on every rank"})
         del rg
     if world >= 4:
         del A, S, B
@@ -1225,12 +1229,12 @@ def run_dmrg(args, torch, ndt, peaks, world=1, rank=0, pg=None):
     D = 1024
     T = ndt.TensorF64
     host = list(W.cfg3_tensors(D))
-    if world > 1:
-        a0, a1 = rank * D // world, (rank + 1) * D // world
-        host[0] = np.asfortranarray(host[0][a0:a1])
     ts = [T.from_numpy(x) for x in host]
     for t in ts:
         t.device_ptr()
+    if world > 1:  # this rank's slab of L, for the host check below
+        a0, a1 = rank * D // world, (rank + 1) * D // world
+        host[0] = np.asfortranarray(host[0][a0:a1])
     L, psi, W1, W2, R = ts
     rhs = [psi, W1, W2, R]
     flops = W.cfg3_flops(D)
@@ -1240,7 +1244,11 @@ def run_dmrg(args, torch, ndt, peaks, world=1, rank=0, pg=None):
         for i, ((la, lb), b) in enumerate(zip(W.CFG3_STEPS, rhs)):
             if ev:
                 ev[i][0].record()
-            cur = ndt.contract_gemm(cur, la, b, lb)
+            if i == 0 and world > 1:
+                # the library's dense split: this rank's range of the free index a
+                cur = ndt.contract_gemm_shard(cur, la, b, lb, 1, rank, world)
+            else:
+                cur = ndt.contract_gemm(cur, la, b, lb)
             if ev:
                 ev[i][1].record()
         return cur

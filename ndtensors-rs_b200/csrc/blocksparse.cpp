@@ -771,7 +771,7 @@ BlockSparseT bs_contract_diag(const BlockSparseT& A, const std::vector<int32_t>&
 // with B (one axis); every other label of A and B is positive.  The result is
 // contract(contract_diag(A, la, S, (x, P)), sorted(A's labels) ++ (y), B, lb)
 // for a fresh positive P, i.e. the A-free ++ B-free axes in label order.
-// Sharded (nranks > 1), when S's blocks are square and each of A's
+// When S's blocks are square and each of A's
 // coordinates on the contracted axis meets at most one S block, this is ONE
 // grouped launch that applies S's diagonal to the contracted index as it
 // loads the operands (no A . S intermediate); otherwise the two
@@ -822,12 +822,10 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
     if (t.bsz[0][qa] != t.bsz[1][qb] || td.qmap.count(qa)) fused = false;
     td.qmap[qa] = {qb, (int64_t)t.offs[b]};
   }
-  // Unsharded, one pass over A (HBM bound, 2 |A| bytes) costs less than
-  // applying S inside the GEMM (6-8% of the c128 GEMM); sharded, every rank
-  // would pay that whole pass for its 1/nranks of the work (c128 MPS chain at
-  // bond 8192: unsharded 1.57 ms two-step against 1.64 fused, 8 ranks
-  // 0.23 ms fused against 0.26 two-step).
-  if (nranks == 1) fused = false;
+  // One launch whenever the structure allows: applying S inside the GEMM
+  // (to B's fragments as they leave shared memory, one multiply per
+  // component for a real diagonal) costs less than a pass of its own over A,
+  // which a sharded rank would pay in full for its 1/nranks of the work.
   if (fused) {
     td.sdata = t.nnzb() ? t.st->dev_read() : nullptr;
     td.real = S.real_valued;
