@@ -20,6 +20,7 @@
 #include <cmath>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <set>
 #include <unordered_map>
 
@@ -181,28 +182,96 @@ struct ThroughDiag {
 constexpr int kGatherChunks = 3;
 constexpr int kGatherSmReserve = 16;
 
+// Host plan of one block-sparse contraction: everything contract_blocksparse
+// derives from the operands' structures and labels (the pair join, the output
+// structure and its owners, operand layouts, the grouped launches' tables,
+// the transfers of a gathered contraction).  Plans are cached by that
+// structure, so repeated contractions of one structure (a sweep over a tensor
+// network, a benchmark loop) pay no host planning: one lookup, the launch.
+struct PlannedLaunch {
+  std::vector<GroupedProblem> probs;
+  std::vector<GroupedSegment> segs;
+  struct Xfer {
+    bool send;
+    int peer;
+    size_t off, elems;  // in elements of the output
+  };
+  std::vector<Xfer> xfers;  // gathered mode: this chunk's transfers
+};
+struct ContractPlan {
+  BlockSparseT c;  // output structure (no storage)
+  bool zero = false;        // nothing to compute: the output is all zeros
+  bool a_kmajor = false, b_kmajor = true;
+  bool pack_a = false, pack_b = false;  // operand blocks permuted to [free, contracted] first
+  std::vector<size_t> perm_a, perm_b;
+  bool permute_c = false;
+  std::vector<size_t> perm_c;
+  bool has_td = false;
+  std::vector<PlannedLaunch> launches;
+};
+
+namespace {
+
+std::mutex g_bsplan_mu;
+std::map<std::vector<int64_t>, std::pair<std::shared_ptr<const ContractPlan>, uint64_t>> g_bsplans;
+uint64_t g_bsplan_tick = 0;
+constexpr size_t kBsPlanCacheSize = 64;
+
+void key_push(std::vector<int64_t>& k, const std::vector<std::vector<size_t>>& vv) {
+  k.push_back((int64_t)vv.size());
+  for (const auto& v : vv) {
+    k.push_back((int64_t)v.size());
+    for (size_t x : v) k.push_back((int64_t)x);
+  }
+}
+
+}  // namespace
+
 // `select` (nsel output coordinates of rank |ua| + |ub|, natural order):
 // compute only those output blocks (the ones the pairs produce), e.g. one
 // rank's share when its operands hold only the blocks that share references.
-// `gcomm` (gathered mode): rank and nranks are the communicator's; this rank
-// computes its share of the output blocks straight into their places in the
-// whole output, and every rank receives the other ranks' blocks there over
-// NCCL (point-to-point, no padding, no assembly copy), chunk by chunk behind
-// the compute.  The result is the unsharded tensor on every rank.
-BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
-                         const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
-                         const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr,
-                         Comm* gcomm = nullptr) {
-  if (gcomm) {
-    rank = comm_rank(*gcomm);
-    nranks = comm_size(*gcomm);
-    if (comm_device(*gcomm) != current_device())
-      throw Error(ErrKind::InvalidArgument, "the communicator belongs to another device than the current one");
-  }
+// `gathered`: every output block is kept in the output, this rank computes
+// its share into their places, and the plan lists the transfers that bring
+// the others' blocks (chunk by chunk, see kGatherChunks).
+std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const std::vector<int32_t>& la,
+                                                  const BlockSparseT& B, const std::vector<int32_t>& lb, int rank,
+                                                  int nranks, ShardPlan* plan_only, const size_t* select, size_t nsel,
+                                                  const ThroughDiag* td, bool gathered) {
   const size_t na = A.ndim(), nb = B.ndim();
   if (A.dt != B.dt) throw Error(ErrKind::InvalidArgument, "element types differ");
   if (la.size() != na) throw Error(ErrKind::WrongNumberOfIndices, "labels_a length != ndim(a)");
   if (lb.size() != nb) throw Error(ErrKind::WrongNumberOfIndices, "labels_b length != ndim(b)");
+  // ---- cache lookup (plan_only queries and selections are not cached)
+  std::vector<int64_t> key;
+  const bool cached = !plan_only && !select;
+  if (cached) {
+    key.push_back((int64_t)A.dt);
+    key.push_back(rank);
+    key.push_back(nranks);
+    key.push_back(gathered ? 1 : 0);
+    key.push_back((int64_t)la.size());
+    for (int32_t l : la) key.push_back(l);
+    key.push_back((int64_t)lb.size());
+    for (int32_t l : lb) key.push_back(l);
+    key_push(key, A.bsz);
+    key_push(key, A.coords);
+    key_push(key, B.bsz);
+    key_push(key, B.coords);
+    key.push_back(td ? (int64_t)td->a_axis : -1);
+    if (td)
+      for (const auto& kv : td->qmap) {
+        key.push_back((int64_t)kv.first);
+        key.push_back((int64_t)kv.second.first);
+        key.push_back(kv.second.second);
+      }
+    std::lock_guard<std::mutex> lk(g_bsplan_mu);
+    auto it = g_bsplans.find(key);
+    if (it != g_bsplans.end()) {
+      it->second.second = ++g_bsplan_tick;
+      return it->second.first;
+    }
+  }
+  auto P = std::make_shared<ContractPlan>();
   // ContractionProperties pairs: first match in B (properties.rs:100-111)
   std::vector<size_t> pa, pb, ua, ub;
   for (size_t i = 0; i < na; i++) {
@@ -229,8 +298,9 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     for (size_t q = 0; q < A.bsz[pa[p]].size(); q++)
       if (A.bsz[pa[p]][q] != B.bsz[pb[p]][q]) throw Error(ErrKind::ShapeMismatch, "block sizes differ");
   }
+  P->has_td = td_pos != SIZE_MAX;
   // output BlockDims (blocksparse.rs:186-209)
-  BlockSparseT C;
+  BlockSparseT& C = P->c;
   C.dt = A.dt;
   for (size_t i : ua) C.bsz.push_back(A.bsz[i]);
   for (size_t j : ub) C.bsz.push_back(B.bsz[j]);
@@ -246,13 +316,13 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   for (size_t b = 0; b < B.nnzb(); b++) bmap[key_of(B.coords[b], pb)].push_back(b);
   std::map<std::vector<size_t>, std::vector<std::pair<size_t, size_t>>> contrib;  // sorted output blocks
   for (size_t a = 0; a < A.nnzb(); a++) {
-    std::vector<size_t> key = key_of(A.coords[a], pa);
+    std::vector<size_t> k = key_of(A.coords[a], pa);
     if (td_pos != SIZE_MAX) {  // through the diagonal: A's q_a meets B's q_b
-      auto q = td->qmap.find(key[td_pos]);
+      auto q = td->qmap.find(k[td_pos]);
       if (q == td->qmap.end()) continue;
-      key[td_pos] = q->second.first;
+      k[td_pos] = q->second.first;
     }
-    auto it = bmap.find(key);
+    auto it = bmap.find(k);
     if (it == bmap.end()) continue;
     for (size_t b : it->second) {
       std::vector<size_t> oc;
@@ -293,12 +363,12 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   std::vector<int32_t> olab;
   for (size_t i : ua) olab.push_back(la[i]);
   for (size_t j : ub) olab.push_back(lb[j]);
-  std::vector<size_t> perm_c(olab.size());
+  std::vector<size_t>& perm_c = P->perm_c;
+  perm_c.resize(olab.size());
   for (size_t i = 0; i < perm_c.size(); i++) perm_c[i] = i;
   std::stable_sort(perm_c.begin(), perm_c.end(), [&](size_t x, size_t y) { return olab[x] < olab[y]; });
-  bool permute_c = false;
   for (size_t i = 0; i < perm_c.size(); i++)
-    if (olab[perm_c[i]] != olab[i]) permute_c = true;
+    if (olab[perm_c[i]] != olab[i]) P->permute_c = true;
 
   // sorted output blocks with their real flops and their cost on the
   // tensor cores: tiles of 64 x 64, k in steps of 16 (a block much smaller
@@ -343,15 +413,15 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
       plan_only->blocks[owner[i]]++;
       plan_only->flops[owner[i]] += work[i];
     }
-    return C;
+    return P;
   }
-  if (gcomm) {
+  if (gathered) {
     C.coords = all_out;
   } else {
     for (size_t i = 0; i < all_out.size(); i++)
       if (owner[i] == rank) C.coords.push_back(all_out[i]);
   }
-  if (nranks > 1 && !gcomm) {
+  if (nranks > 1 && !gathered) {
     auto lay = std::make_shared<ShardLayout>();
     lay->nranks = nranks;
     lay->coords = all_out;
@@ -359,161 +429,205 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     C.layout = lay;
   }
   C.pack();
-  C.st = std::make_shared<Storage>(C.dt, C.total());
   if (C.total() == 0 || contrib.empty()) {
+    P->zero = true;
+  } else {
+    // insertblock shape check for the first contribution (blocksparse_tensor.rs:218-223)
+    for (size_t ob = 0; ob < C.nnzb(); ob++) {
+      std::vector<size_t> sh = C.block_shape(C.coords[ob]);
+      if (P->permute_c) {
+        std::vector<size_t> sorted(sh.size());
+        for (size_t i = 0; i < sh.size(); i++) sorted[i] = sh[perm_c[i]];
+        if (sorted != sh) throw Error(ErrKind::ShapeMismatch, "contract_gemm block shape differs from output block");
+      }
+    }
+    for (size_t ob = 0; ob < C.nnzb(); ob++)
+      for (auto& pr : contrib[C.coords[ob]]) {
+        if (A.block_elems(A.coords[pr.first]) == 0 || B.block_elems(B.coords[pr.second]) == 0)
+          throw Error(ErrKind::Panic, "zero-size block in a contracted pair");
+      }
+    // operand layouts at the tensor level
+    if (is_prefix_run(ua, 0) && is_prefix_run(pa, ua.size())) {
+      P->a_kmajor = false;
+    } else if (is_prefix_run(pa, 0) && is_prefix_run(ua, pa.size())) {
+      P->a_kmajor = true;
+    } else {
+      P->perm_a = ua;
+      P->perm_a.insert(P->perm_a.end(), pa.begin(), pa.end());
+      P->pack_a = true;
+      P->a_kmajor = false;
+    }
+    if (is_prefix_run(pb, 0) && is_prefix_run(ub, pb.size())) {
+      P->b_kmajor = true;
+    } else if (is_prefix_run(ub, 0) && is_prefix_run(pb, ub.size())) {
+      P->b_kmajor = false;
+    } else {
+      P->perm_b = pb;
+      P->perm_b.insert(P->perm_b.end(), ub.begin(), ub.end());
+      P->pack_b = true;
+      P->b_kmajor = true;
+    }
+    // device tables: one problem per output block, one segment per pair
+    auto make_table = [&](const std::vector<size_t>& obs, PlannedLaunch& L) {
+      for (size_t ob : obs) {
+        const auto& prs = contrib[C.coords[ob]];
+        GroupedProblem pr{};
+        int64_t m = 1, n = 1;
+        for (size_t i : ua) m *= (int64_t)A.bsz[i][A.coords[prs[0].first][i]];
+        for (size_t j : ub) n *= (int64_t)B.bsz[j][B.coords[prs[0].second][j]];
+        pr.m = m;
+        pr.n = n;
+        pr.c_off = (int64_t)C.offs[ob];
+        pr.seg_begin = (int64_t)L.segs.size();
+        pr.seg_count = (int64_t)prs.size();
+        for (auto& p2 : prs) {
+          GroupedSegment sg{};
+          int64_t k = 1;
+          for (size_t i : pa) k *= (int64_t)A.bsz[i][A.coords[p2.first][i]];
+          sg.a_off = (int64_t)A.offs[p2.first];
+          sg.b_off = (int64_t)B.offs[p2.second];
+          sg.k = k;
+          sg.lda = P->a_kmajor ? k : m;
+          sg.ldb = P->b_kmajor ? k : n;
+          sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
+          L.segs.push_back(sg);
+        }
+        L.probs.push_back(pr);
+      }
+    };
+    if (!gathered) {
+      std::vector<size_t> obs(C.nnzb());
+      for (size_t i = 0; i < obs.size(); i++) obs[i] = i;
+      P->launches.emplace_back();
+      make_table(obs, P->launches.back());
+    } else {
+      // Chunks: every rank's blocks by descending tile cost, dealt round-robin
+      // (every rank derives the same chunk of every block, so each transfer's
+      // sender and receiver issue it in the same group, in block order).
+      std::vector<int> chunk(all_out.size(), 0);
+      {
+        std::vector<size_t> order(all_out.size());
+        for (size_t i = 0; i < order.size(); i++) order[i] = i;
+        std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return cost[x] > cost[y]; });
+        std::vector<int> dealt(nranks, 0);
+        for (size_t i : order) chunk[i] = dealt[owner[i]]++ % kGatherChunks;
+      }
+      for (int c = 0; c < kGatherChunks; c++) {
+        P->launches.emplace_back();
+        PlannedLaunch& L = P->launches.back();
+        std::vector<size_t> mine;
+        for (size_t i = 0; i < all_out.size(); i++)
+          if (owner[i] == rank && chunk[i] == c) mine.push_back(i);
+        make_table(mine, L);
+        // this chunk's blocks: runs of consecutive blocks (contiguous in the
+        // packed output) with one owner; the owner sends, the others receive
+        for (size_t i = 0; i < all_out.size();) {
+          if (chunk[i] != c) {
+            i++;
+            continue;
+          }
+          size_t j = i + 1;
+          while (j < all_out.size() && chunk[j] == c && owner[j] == owner[i]) j++;
+          const size_t off = C.offs[i], n = C.offs[j] - C.offs[i];
+          if (owner[i] == rank) {
+            for (int q = 0; q < nranks; q++)
+              if (q != rank) L.xfers.push_back({true, q, off, n});
+          } else {
+            L.xfers.push_back({false, owner[i], off, n});
+          }
+          i = j;
+        }
+      }
+    }
+  }
+  if (cached) {
+    std::lock_guard<std::mutex> lk(g_bsplan_mu);
+    if (g_bsplans.size() >= kBsPlanCacheSize) {
+      auto victim = g_bsplans.begin();
+      for (auto it = g_bsplans.begin(); it != g_bsplans.end(); ++it)
+        if (it->second.second < victim->second.second) victim = it;
+      g_bsplans.erase(victim);
+    }
+    g_bsplans[key] = {P, ++g_bsplan_tick};
+  }
+  return P;
+}
+
+// contract_blocksparse (contract/blocksparse.rs:87-183), planned by
+// plan_contract and run as grouped launches (one, or one per chunk of a
+// gathered contraction).  With nranks > 1 only this rank's output blocks are
+// computed and stored (longest processing time on the tile cost; every rank
+// derives the same assignment).  `gcomm` (gathered mode): rank and nranks are
+// the communicator's; this rank computes its share of the output blocks
+// straight into their places in the whole output, and every rank receives
+// the other ranks' blocks there over NCCL (point-to-point, no padding, no
+// assembly copy), chunk by chunk behind the compute.  The result is the
+// unsharded tensor on every rank.
+BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
+                         const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
+                         const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr,
+                         Comm* gcomm = nullptr) {
+  if (gcomm) {
+    rank = comm_rank(*gcomm);
+    nranks = comm_size(*gcomm);
+    if (comm_device(*gcomm) != current_device())
+      throw Error(ErrKind::InvalidArgument, "the communicator belongs to another device than the current one");
+  }
+  std::shared_ptr<const ContractPlan> P =
+      plan_contract(A, la, B, lb, rank, nranks, plan_only, select, nsel, td, gcomm != nullptr);
+  if (plan_only) return P->c;
+  BlockSparseT C = P->c;
+  C.st = std::make_shared<Storage>(C.dt, C.total());
+  if (P->zero) {
     C.st->set_uniform(0.0, 0.0);
     return C;
   }
-  // insertblock shape check for the first contribution (blocksparse_tensor.rs:218-223)
-  for (size_t ob = 0; ob < C.nnzb(); ob++) {
-    std::vector<size_t> sh = C.block_shape(C.coords[ob]);
-    if (permute_c) {
-      std::vector<size_t> sorted(sh.size());
-      for (size_t i = 0; i < sh.size(); i++) sorted[i] = sh[perm_c[i]];
-      if (sorted != sh) throw Error(ErrKind::ShapeMismatch, "contract_gemm block shape differs from output block");
-    }
-  }
-  for (size_t ob = 0; ob < C.nnzb(); ob++)
-    for (auto& pr : contrib[C.coords[ob]]) {
-      if (A.block_elems(A.coords[pr.first]) == 0 || B.block_elems(B.coords[pr.second]) == 0)
-        throw Error(ErrKind::Panic, "zero-size block in a contracted pair");
-    }
-
   const DeviceCtx& c = ctx();
   cudaStream_t s = c.compute;
   const int dev = current_device();
   const size_t es = esize(A.dt);
-  // operand layouts at the tensor level
   const void* Ad = A.st->dev_read();
   const void* Bd = B.st->dev_read();
   void* Aown = nullptr;
   void* Bown = nullptr;
-  bool a_kmajor = false, b_kmajor = true;
-  if (is_prefix_run(ua, 0) && is_prefix_run(pa, ua.size())) {
-    a_kmajor = false;
-  } else if (is_prefix_run(pa, 0) && is_prefix_run(ua, pa.size())) {
-    a_kmajor = true;
-  } else {
-    std::vector<size_t> perm(ua);
-    perm.insert(perm.end(), pa.begin(), pa.end());
+  if (P->pack_a) {
     std::vector<size_t> order(A.nnzb());
     for (size_t i = 0; i < order.size(); i++) order[i] = i;
     Aown = dev_alloc(A.total() * es, dev);
-    permute_blocks(A.dt, Ad, Aown, A, perm, A.offs, order, s);
+    permute_blocks(A.dt, Ad, Aown, A, P->perm_a, A.offs, order, s);
     Ad = Aown;
-    a_kmajor = false;
   }
-  if (is_prefix_run(pb, 0) && is_prefix_run(ub, pb.size())) {
-    b_kmajor = true;
-  } else if (is_prefix_run(ub, 0) && is_prefix_run(pb, ub.size())) {
-    b_kmajor = false;
-  } else {
-    std::vector<size_t> perm(pb);
-    perm.insert(perm.end(), ub.begin(), ub.end());
+  if (P->pack_b) {
     std::vector<size_t> order(B.nnzb());
     for (size_t i = 0; i < order.size(); i++) order[i] = i;
     Bown = dev_alloc(B.total() * es, dev);
-    permute_blocks(B.dt, Bd, Bown, B, perm, B.offs, order, s);
+    permute_blocks(B.dt, Bd, Bown, B, P->perm_b, B.offs, order, s);
     Bd = Bown;
-    b_kmajor = true;
   }
-  // device table: one problem per output block, one segment per pair
-  auto make_table = [&](const std::vector<size_t>& obs, std::vector<GroupedProblem>& probs,
-                        std::vector<GroupedSegment>& segs) {
-    for (size_t ob : obs) {
-      const auto& prs = contrib[C.coords[ob]];
-      GroupedProblem pr{};
-      int64_t m = 1, n = 1;
-      for (size_t i : ua) m *= (int64_t)A.bsz[i][A.coords[prs[0].first][i]];
-      for (size_t j : ub) n *= (int64_t)B.bsz[j][B.coords[prs[0].second][j]];
-      pr.m = m;
-      pr.n = n;
-      pr.c_off = (int64_t)C.offs[ob];
-      pr.seg_begin = (int64_t)segs.size();
-      pr.seg_count = (int64_t)prs.size();
-      for (auto& p2 : prs) {
-        GroupedSegment sg{};
-        int64_t k = 1;
-        for (size_t i : pa) k *= (int64_t)A.bsz[i][A.coords[p2.first][i]];
-        sg.a_off = (int64_t)A.offs[p2.first];
-        sg.b_off = (int64_t)B.offs[p2.second];
-        sg.k = k;
-        sg.lda = a_kmajor ? k : m;
-        sg.ldb = b_kmajor ? k : n;
-        sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
-        segs.push_back(sg);
-      }
-      probs.push_back(pr);
-    }
-  };
   void* Cd = C.st->dev_overwrite();
-  void* Cu = permute_c ? dev_alloc(C.total() * es, dev) : Cd;
-  const void* kscale = td_pos != SIZE_MAX ? td->sdata : nullptr;
-  const bool kreal = td_pos != SIZE_MAX && td->real;
-  if (!gcomm) {
-    std::vector<size_t> obs(C.nnzb());
-    for (size_t i = 0; i < obs.size(); i++) obs[i] = i;
-    std::vector<GroupedProblem> probs;
-    std::vector<GroupedSegment> segs;
-    make_table(obs, probs, segs);
-    grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, kscale, s, kreal);
-  } else {
-    // Chunks: every rank's blocks by descending tile cost, dealt round-robin
-    // (every rank derives the same chunk of every block, so each transfer's
-    // sender and receiver issue it in the same group, in block order).
-    std::vector<int> chunk(all_out.size(), 0);
-    {
-      std::vector<size_t> order(all_out.size());
-      for (size_t i = 0; i < order.size(); i++) order[i] = i;
-      std::stable_sort(order.begin(), order.end(), [&](size_t x, size_t y) { return cost[x] > cost[y]; });
-      std::vector<int> dealt(nranks, 0);
-      for (size_t i : order) chunk[i] = dealt[owner[i]]++ % kGatherChunks;
-    }
-    const size_t dpe = es / 8;  // doubles per element
-    Comm& cm = *gcomm;
-    for (int c = 0; c < kGatherChunks; c++) {
-      std::vector<size_t> mine;
-      for (size_t i = 0; i < all_out.size(); i++)
-        if (owner[i] == rank && chunk[i] == c) mine.push_back(i);
-      if (!mine.empty()) {
-        std::vector<GroupedProblem> probs;
-        std::vector<GroupedSegment> segs;
-        make_table(mine, probs, segs);
-        grouped_gemm(A.dt, Ad, Bd, Cu, a_kmajor, b_kmajor, probs, segs, kscale, s, kreal,
-                     nranks > 1 ? kGatherSmReserve : 0);
-      }
-      // this chunk's blocks: runs of consecutive blocks (contiguous in the
-      // packed output) with one owner; the owner sends, the others receive
+  void* Cu = P->permute_c ? dev_alloc(C.total() * es, dev) : Cd;
+  const void* kscale = P->has_td ? td->sdata : nullptr;
+  const bool kreal = P->has_td && td->real;
+  for (const PlannedLaunch& L : P->launches) {
+    if (!L.probs.empty())
+      grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
+                   gcomm && nranks > 1 ? kGatherSmReserve : 0);
+    if (gcomm) {
       std::vector<P2POp> ops;
-      for (size_t i = 0; i < all_out.size();) {
-        if (chunk[i] != c) {
-          i++;
-          continue;
-        }
-        size_t j = i + 1;
-        while (j < all_out.size() && chunk[j] == c && owner[j] == owner[i]) j++;
-        char* p = (char*)Cu + C.offs[i] * es;
-        const size_t nd = (C.offs[j] - C.offs[i]) * dpe;
-        if (owner[i] == rank) {
-          for (int q = 0; q < nranks; q++)
-            if (q != rank) ops.push_back(P2POp{true, q, p, nd});
-        } else {
-          ops.push_back(P2POp{false, owner[i], p, nd});
-        }
-        i = j;
-      }
-      comm_exchange(cm, ops, s, nullptr);
+      ops.reserve(L.xfers.size());
+      for (const auto& x : L.xfers)
+        ops.push_back(P2POp{x.send, x.peer, (char*)Cu + x.off * es, x.elems * (es / 8)});
+      comm_exchange(*gcomm, ops, s, nullptr);
     }
-    comm_join(cm, s);
   }
-  if (permute_c) {
+  if (gcomm) comm_join(*gcomm, s);
+  if (P->permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,
-    // checked above); the data is permuted block by block.
-    BlockSparseT tmp = C;
+    // checked in the plan); the data is permuted block by block.
     std::vector<size_t> order(C.nnzb());
     for (size_t i = 0; i < order.size(); i++) order[i] = i;
     // blocks of Cu are laid out in the unsorted axis order [A free..., B free...]
-    permute_blocks(C.dt, Cu, Cd, tmp, perm_c, C.offs, order, s);
+    permute_blocks(C.dt, Cu, Cd, C, P->perm_c, C.offs, order, s);
     dev_free(Cu, dev);
   }
   if (Aown) dev_free(Aown, dev);
