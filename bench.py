@@ -828,20 +828,24 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     bs = ndt.blocksparse
     out = []
 
-    def timed(fn, reps, warm=2):
+    def timed(fn, reps, warm=3, groups=3):
+        """Median over `groups` runs of `reps` back-to-back calls (ms per call)."""
         for _ in range(warm):
             r = fn()
         r = None  # the timed calls reuse the warm-up's memory instead of growing the pool
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            r = fn()
-        e1.record()
-        torch.cuda.synchronize()
-        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+        per = []
+        for _ in range(groups):
+            if pg:
+                pg.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                r = fn()
+            e1.record()
+            torch.cuda.synchronize()
+            per.append(e0.elapsed_time(e1) / reps)
+        t = torch.tensor([statistics.median(per)], device="cuda")
         if pg:
             pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t.item()), r
@@ -859,9 +863,9 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
     la, lb = [1, 2, -1, -2], [-1, -2, 3, 4]
     flops = W.flops_blocksparse((sizes, coords, None), la, (sizes, coords, None), lb, False)
     if world == 1:
-        ms, r = timed(lambda: bs.contract(A, la, B, lb), 3)
+        ms, r = timed(lambda: bs.contract(A, la, B, lb), 3, warm=2, groups=1)
     else:
-        ms, r = timed(lambda: bs.contract_shard(A, la, B, lb, rank, world), 3)
+        ms, r = timed(lambda: bs.contract_shard(A, la, B, lb, rank, world), 3, warm=2, groups=1)
     # the timed result checked against the CPU block reference (the operands
     # stay on the device; only the blocks a sampled pair uses are copied)
     par = block_parity(torch, bs, r, (sizes, coords, dA), (sizes, coords, dB), 2, 2, world)
@@ -989,7 +993,7 @@ def literal_u1_rank4(torch, ndt, W, world, rank, timed):
     A, ka = make(used_a, 1)
     B, kb = make(used_b, 2)
     torch.cuda.synchronize()
-    ms, r = timed(lambda: bs.contract_select(A, la, B, lb, mine), 1, warm=1)
+    ms, r = timed(lambda: bs.contract_select(A, la, B, lb, mine), 1, warm=1, groups=1)
     tf = total / (ms * 1e-3) / 1e12
     # a sample of this rank's output blocks against the CPU block reference,
     # within 3e11 flop of host work per rank (the largest blocks are 1e13)
