@@ -913,7 +913,7 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
         out.append({"cfg": "c5 c128 MPS+gather", "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "ms": msg, "n_gpus": world, "scaling": "strong", "parity": parg,
                     "gather": "gathered in the library (ndt_blocksparse_c64_contract_through_diag_gathered): "
-                              "NCCL point to point into the output's block offsets, chunked behind the compute",
+                              "an NCCL all-gather per chunk behind the next chunk's compute, one copy into the sorted output",
                     "workload": "block-sparse c128 two-site MPS, sharded + gathered on every rank"})
         del rg
     if world >= 4:

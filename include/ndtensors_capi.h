@@ -384,9 +384,10 @@ void ndt_b200_comm_release(ndt_comm* comm);
 /* contract_blocksparse with the output gathered on every rank (the contract
  * "gather" flag; device list = the communicator's ranks).  Every rank passes
  * the same operands; each computes its share of the output blocks (longest
- * processing time on tile cost, as contract_shard) straight into their places
- * in the packed, sorted output and receives the others' blocks there over
- * NCCL point to point, chunk by chunk while it computes.  Every rank returns
+ * processing time on tile cost, as contract_shard) into its slot of a staging
+ * buffer, chunk by chunk; an NCCL all-gather per chunk runs while the next
+ * chunk computes, and one copy kernel puts every block at its place in the
+ * packed, sorted output.  Every rank returns
  * the unsharded result (same structure and values as
  * ndt_blocksparse_*_contract).  Collective: every rank of the communicator
  * must call it, with the same arguments. */

@@ -191,12 +191,9 @@ constexpr int kGatherSmReserve = 16;
 struct PlannedLaunch {
   std::vector<GroupedProblem> probs;
   std::vector<GroupedSegment> segs;
-  struct Xfer {
-    bool send;
-    int peer;
-    size_t off, elems;  // in elements of the output
-  };
-  std::vector<Xfer> xfers;  // gathered mode: this chunk's transfers
+  // gathered mode: this chunk's region of the staging buffer (elements):
+  // rank r's blocks of the chunk, packed, at stage_off + r * pad
+  size_t stage_off = 0, pad = 0;
 };
 struct ContractPlan {
   BlockSparseT c;  // output structure (no storage)
@@ -208,6 +205,10 @@ struct ContractPlan {
   std::vector<size_t> perm_c;
   bool has_td = false;
   std::vector<PlannedLaunch> launches;
+  // gathered mode: staging size (elements) and the copy that moves every
+  // block from its staging place to its place in the sorted output (bytes)
+  size_t stage_total = 0;
+  std::vector<int64_t> copy_src, copy_dst, copy_bytes;
 };
 
 namespace {
@@ -512,31 +513,45 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
         std::vector<int> dealt(nranks, 0);
         for (size_t i : order) chunk[i] = dealt[owner[i]]++ % kGatherChunks;
       }
+      // Staging layout, chunk-major then rank-major: chunk c's region holds
+      // nranks slots of pad_c elements (pad_c: the largest rank's chunk c),
+      // rank r's blocks of the chunk packed in sorted order in slot r.  Each
+      // rank computes its blocks into its own slot; an in-place all-gather
+      // per chunk fills the others; one copy puts every block at its place.
+      const size_t es = esize(A.dt);
+      std::vector<size_t> stage_of(all_out.size(), 0);
+      size_t off = 0;
       for (int c = 0; c < kGatherChunks; c++) {
         P->launches.emplace_back();
         PlannedLaunch& L = P->launches.back();
+        std::vector<size_t> fill(nranks, 0);
+        for (size_t i = 0; i < all_out.size(); i++)
+          if (chunk[i] == c) fill[owner[i]] += C.offs[i + 1] - C.offs[i];
+        size_t pad = 0;
+        for (size_t f : fill) pad = std::max(pad, f);
+        pad = (pad + 1) / 2 * 2;  // slots start 16-byte aligned (f64)
+        L.stage_off = off;
+        L.pad = pad;
+        std::fill(fill.begin(), fill.end(), 0);
+        for (size_t i = 0; i < all_out.size(); i++)
+          if (chunk[i] == c) {
+            stage_of[i] = off + (size_t)owner[i] * pad + fill[owner[i]];
+            fill[owner[i]] += C.offs[i + 1] - C.offs[i];
+          }
+        off += (size_t)nranks * pad;
         std::vector<size_t> mine;
         for (size_t i = 0; i < all_out.size(); i++)
           if (owner[i] == rank && chunk[i] == c) mine.push_back(i);
         make_table(mine, L);
-        // this chunk's blocks: runs of consecutive blocks (contiguous in the
-        // packed output) with one owner; the owner sends, the others receive
-        for (size_t i = 0; i < all_out.size();) {
-          if (chunk[i] != c) {
-            i++;
-            continue;
-          }
-          size_t j = i + 1;
-          while (j < all_out.size() && chunk[j] == c && owner[j] == owner[i]) j++;
-          const size_t off = C.offs[i], n = C.offs[j] - C.offs[i];
-          if (owner[i] == rank) {
-            for (int q = 0; q < nranks; q++)
-              if (q != rank) L.xfers.push_back({true, q, off, n});
-          } else {
-            L.xfers.push_back({false, owner[i], off, n});
-          }
-          i = j;
-        }
+        for (size_t q = 0; q < mine.size(); q++) L.probs[q].c_off = (int64_t)stage_of[mine[q]];
+      }
+      P->stage_total = off;
+      for (size_t i = 0; i < all_out.size(); i++) {
+        const size_t n = C.offs[i + 1] - C.offs[i];
+        if (!n) continue;
+        P->copy_src.push_back((int64_t)(stage_of[i] * es));
+        P->copy_dst.push_back((int64_t)(C.offs[i] * es));
+        P->copy_bytes.push_back((int64_t)(n * es));
       }
     }
   }
@@ -558,11 +573,11 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
 // gathered contraction).  With nranks > 1 only this rank's output blocks are
 // computed and stored (longest processing time on the tile cost; every rank
 // derives the same assignment).  `gcomm` (gathered mode): rank and nranks are
-// the communicator's; this rank computes its share of the output blocks
-// straight into their places in the whole output, and every rank receives
-// the other ranks' blocks there over NCCL (point-to-point, no padding, no
-// assembly copy), chunk by chunk behind the compute.  The result is the
-// unsharded tensor on every rank.
+// the communicator's; this rank computes its share of the output blocks into
+// its slot of a staging buffer, chunk by chunk, an NCCL all-gather per chunk
+// runs behind the next chunk's compute, and one copy kernel puts every block
+// at its place in the sorted output.  The result is the unsharded tensor on
+// every rank.
 BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
                          const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
                          const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr,
@@ -608,19 +623,18 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   void* Cu = P->permute_c ? dev_alloc(C.total() * es, dev) : Cd;
   const void* kscale = P->has_td ? td->sdata : nullptr;
   const bool kreal = P->has_td && td->real;
+  void* stage = gcomm ? dev_alloc(P->stage_total * es, dev) : nullptr;
   for (const PlannedLaunch& L : P->launches) {
     if (!L.probs.empty())
-      grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
+      grouped_gemm(A.dt, Ad, Bd, gcomm ? stage : Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
                    gcomm && nranks > 1 ? kGatherSmReserve : 0);
-    if (gcomm) {
-      std::vector<P2POp> ops;
-      ops.reserve(L.xfers.size());
-      for (const auto& x : L.xfers)
-        ops.push_back(P2POp{x.send, x.peer, (char*)Cu + x.off * es, x.elems * (es / 8)});
-      comm_exchange(*gcomm, ops, s, nullptr);
-    }
+    if (gcomm) comm_allgather(*gcomm, (char*)stage + L.stage_off * es, L.pad * (es / 8), s);
   }
-  if (gcomm) comm_join(*gcomm, s);
+  if (gcomm) {
+    comm_join(*gcomm, s);
+    copy_segments(stage, Cu, P->copy_src, P->copy_dst, P->copy_bytes, s);
+    dev_free(stage, dev);
+  }
   if (P->permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,
     // checked in the plan); the data is permuted block by block.
@@ -961,10 +975,8 @@ BlockSparseT bs_contract_through_diag(const BlockSparseT& A, const std::vector<i
 }
 
 // The whole output of a sharded contraction on every rank, from this rank's
-// shard (which carries the layout: every output block and its owner).  The
-// rank's own blocks are copied to their places in the packed, sorted output;
-// the others arrive there over NCCL point to point, one transfer per run of
-// consecutive blocks with one owner (no padding, no assembly copy).
+// shard (which carries the layout: every output block and its owner, so no
+// structure is exchanged).
 BlockSparseT bs_allgather(const BlockSparseT& shard, Comm& cm) {
   if (!shard.layout) throw Error(ErrKind::InvalidArgument, "allgather needs a shard of a sharded contraction");
   const ShardLayout& L = *shard.layout;
@@ -980,36 +992,35 @@ BlockSparseT bs_allgather(const BlockSparseT& shard, Comm& cm) {
   if (C.total() == 0) return C;
   const size_t es = esize(C.dt);
   cudaStream_t s = ctx().compute;
+  const int dev = current_device();
   void* d = C.st->dev_overwrite();
-  if (shard.total()) {
-    const void* src = shard.st->dev_read();
-    std::vector<int64_t> so, dso, nb;
-    size_t r = 0;
-    for (size_t i = 0; i < L.coords.size(); i++)
-      if (L.owner[i] == rank) {
-        so.push_back((int64_t)(shard.offs[r] * es));
-        dso.push_back((int64_t)(C.offs[i] * es));
-        nb.push_back((int64_t)(shard.block_elems(shard.coords[r]) * es));
-        r++;
-      }
-    copy_segments(src, d, so, dso, nb, s);
+  // every rank's shard (its blocks, packed in sorted order) in slot r of a
+  // staging buffer of nranks slots of the largest shard's size; one in-place
+  // all-gather, then one copy puts every block at its place
+  std::vector<size_t> per(nranks, 0), pos(L.coords.size(), 0);
+  for (size_t i = 0; i < L.coords.size(); i++) {
+    pos[i] = per[L.owner[i]];
+    per[L.owner[i]] += C.offs[i + 1] - C.offs[i];
   }
-  std::vector<P2POp> ops;
-  const size_t dpe = es / 8;
-  for (size_t i = 0; i < L.coords.size();) {
-    size_t j = i + 1;
-    while (j < L.coords.size() && L.owner[j] == L.owner[i]) j++;
-    char* p = (char*)d + C.offs[i] * es;
-    const size_t n = (C.offs[j] - C.offs[i]) * dpe;
-    if (L.owner[i] == rank) {
-      for (int q = 0; q < nranks; q++)
-        if (q != rank) ops.push_back(P2POp{true, q, p, n});
-    } else {
-      ops.push_back(P2POp{false, L.owner[i], p, n});
-    }
-    i = j;
+  size_t pad = 0;
+  for (size_t x : per) pad = std::max(pad, x);
+  pad = (pad + 1) / 2 * 2;
+  void* stage = dev_alloc((size_t)nranks * pad * es, dev);
+  if (shard.total())
+    NDT_CUDA(cudaMemcpyAsync((char*)stage + (size_t)rank * pad * es, shard.st->dev_read(), shard.total() * es,
+                             cudaMemcpyDeviceToDevice, s));
+  comm_allgather(cm, stage, pad * (es / 8), s);
+  comm_join(cm, s);
+  std::vector<int64_t> so, dso, nb;
+  for (size_t i = 0; i < L.coords.size(); i++) {
+    const size_t n = C.offs[i + 1] - C.offs[i];
+    if (!n) continue;
+    so.push_back((int64_t)(((size_t)L.owner[i] * pad + pos[i]) * es));
+    dso.push_back((int64_t)(C.offs[i] * es));
+    nb.push_back((int64_t)(n * es));
   }
-  comm_exchange(cm, ops, s, s);
+  copy_segments(stage, d, so, dso, nb, s);
+  dev_free(stage, dev);
   return C;
 }
 

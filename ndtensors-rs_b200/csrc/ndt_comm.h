@@ -14,17 +14,10 @@ int comm_rank(const Comm& c);
 int comm_size(const Comm& c);
 int comm_device(const Comm& c);
 
-// One point-to-point transfer of `doubles` doubles at `ptr` to / from `peer`.
-struct P2POp {
-  bool send;
-  int peer;
-  void* ptr;
-  size_t doubles;
-};
-// Enqueue `ops` as one NCCL group on the communicator's stream, after the
-// work enqueued so far on `after`; when `then` is not null it waits for the
-// group.  Sends and receives between two ranks match in the order issued.
-void comm_exchange(Comm& c, const std::vector<P2POp>& ops, cudaStream_t after, cudaStream_t then);
+// In-place all-gather on the communicator's stream, after the work enqueued
+// so far on `after`: rank r's `doubles_per_rank` doubles at
+// buf + r * doubles_per_rank reach every rank at the same place.
+void comm_allgather(Comm& c, void* buf, size_t doubles_per_rank, cudaStream_t after);
 // `s` waits for every transfer enqueued so far on the communicator.
 void comm_join(Comm& c, cudaStream_t s);
 

@@ -410,8 +410,8 @@ class Comm:
     process per GPU.  ``Comm.from_group(group)`` builds it collectively over a
     torch.distributed group: rank 0 creates NCCL's unique id and the group
     broadcasts it.  Used by contract_gathered, contract_through_diag_gathered
-    and allgather, which gather a sharded result in the library (NCCL point to
-    point, straight into the output's block offsets)."""
+    and allgather, which gather a sharded result in the library (an in-place
+    NCCL all-gather, then one copy kernel into the sorted output)."""
 
     _by_group = {}
 
@@ -509,9 +509,9 @@ def allgather(shard, group=None, comm: Comm = None):
     tensors.
 
     With `comm` (or on an NCCL group, for a shard that carries its layout)
-    the library gathers the shard itself: NCCL point-to-point transfers
-    straight into the output's block offsets, no padding and no assembly
-    copy (ndt_blocksparse_*_allgather)."""
+    the library gathers the shard itself (ndt_blocksparse_*_allgather): one
+    in-place NCCL all-gather of the shards, then one copy kernel into the
+    sorted output, with no Python work per block."""
     import torch
     import torch.distributed as dist
 

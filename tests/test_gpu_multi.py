@@ -2,8 +2,8 @@
 
 Each rank computes its cost-balanced share of the output blocks
 (contract_shard, contract_through_diag) and the shards are gathered in HBM
-by the library (allgather over the library's NCCL communicator: point-to-point
-transfers straight into the output's block offsets).  The gathered
+by the library (allgather over the library's NCCL communicator: one in-place
+all-gather, one copy kernel into the sorted output).  The gathered
 contractions of the C ABI (contract_gathered, contract_through_diag_gathered:
 compute and gather chunk by chunk) are checked the same way, and the c128
 chain at bond 8192 block by block against the CPU block reference.  The
