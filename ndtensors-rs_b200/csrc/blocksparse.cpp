@@ -175,12 +175,16 @@ struct ThroughDiag {
   bool real = false;  // every diagonal value real (one multiply per component)
 };
 
-// Overlap of compute and gather in a gathered contraction: each rank's
-// output blocks (by descending tile cost) are dealt round-robin into this
-// many chunks; chunk c's transfers run while chunk c + 1 computes, on SMs
-// that chunk's launch leaves free.
-constexpr int kGatherChunks = 3;
-constexpr int kGatherSmReserve = 16;
+// Gathered contractions where the ranks cannot write into each other's
+// memory (more than kMaxSymRanks ranks, or no CUDA IPC): each rank's output
+// blocks (by descending tile cost) are dealt round-robin into this many
+// chunks, and chunk c's NCCL all-gather may run while chunk c + 1 computes,
+// on SMs that chunk's launch leaves free.  Measured on two B200s (c128 MPS
+// chain, bond 8192): one chunk and no reserved SMs is fastest (1.03 ms; two
+// chunks 1.07, three chunks with 8 or 16 reserved SMs 1.17 / 1.20): NCCL's
+// kernels gain little beside a persistent GEMM that fills every SM.
+constexpr int kGatherChunks = 1;
+constexpr int kGatherSmReserve = 0;
 
 // Host plan of one block-sparse contraction: everything contract_blocksparse
 // derives from the operands' structures and labels (the pair join, the output
@@ -209,6 +213,9 @@ struct ContractPlan {
   // block from its staging place to its place in the sorted output (bytes)
   size_t stage_total = 0;
   std::vector<int64_t> copy_src, copy_dst, copy_bytes;
+  // gathered mode, ranks mapping each other's memory: this rank's blocks at
+  // their places in the sorted output, computed once and stored to every rank
+  PlannedLaunch direct;
 };
 
 namespace {
@@ -546,6 +553,12 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
         for (size_t q = 0; q < mine.size(); q++) L.probs[q].c_off = (int64_t)stage_of[mine[q]];
       }
       P->stage_total = off;
+      {
+        std::vector<size_t> mine;
+        for (size_t i = 0; i < all_out.size(); i++)
+          if (owner[i] == rank) mine.push_back(i);
+        make_table(mine, P->direct);
+      }
       for (size_t i = 0; i < all_out.size(); i++) {
         const size_t n = C.offs[i + 1] - C.offs[i];
         if (!n) continue;
@@ -623,8 +636,26 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   void* Cu = P->permute_c ? dev_alloc(C.total() * es, dev) : Cd;
   const void* kscale = P->has_td ? td->sdata : nullptr;
   const bool kreal = P->has_td && td->real;
+  void* mine = nullptr;
+  std::vector<void*> peers(kMaxSymRanks, nullptr);
+  if (gcomm && nranks > 1 && comm_symmetric(*gcomm, C.total() * es, s, &mine, peers.data())) {
+    // One launch computes this rank's output blocks and stores every tile
+    // into this rank's mapped buffer and into every other rank's, over
+    // NVLink, as it is computed (no separate transfer); a barrier over the
+    // ranks, then the buffer is copied into the result.
+    std::vector<void*> others;
+    for (int r = 0; r < nranks; r++)
+      if (r != rank) others.push_back(peers[r]);
+    if (!P->direct.probs.empty())
+      grouped_gemm(A.dt, Ad, Bd, mine, P->a_kmajor, P->b_kmajor, P->direct.probs, P->direct.segs, kscale, s, kreal,
+                   0, &others);
+    comm_barrier(*gcomm, s, s);
+    NDT_CUDA(cudaMemcpyAsync(Cu, mine, C.total() * es, cudaMemcpyDeviceToDevice, s));
+    gcomm = nullptr;  // done: no staged launches below
+  }
   void* stage = gcomm ? dev_alloc(P->stage_total * es, dev) : nullptr;
   for (const PlannedLaunch& L : P->launches) {
+    if (!gcomm && mine) break;
     if (!L.probs.empty())
       grouped_gemm(A.dt, Ad, Bd, gcomm ? stage : Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
                    gcomm && nranks > 1 ? kGatherSmReserve : 0);

@@ -21,6 +21,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "../../include/ndtensors_capi.h"
 #include "ndt_internal.h"
@@ -38,6 +39,7 @@ struct NcclApi {
   decltype(&ncclCommUserRank) user_rank = nullptr;
   decltype(&ncclCommCuDevice) cu_device = nullptr;
   decltype(&ncclAllGather) all_gather = nullptr;
+  decltype(&ncclAllReduce) all_reduce = nullptr;
   decltype(&ncclGetErrorString) error_string = nullptr;
   decltype(&ncclCommGetAsyncError) async_error = nullptr;
 };
@@ -64,6 +66,7 @@ const NcclApi& api() {
   a->user_rank = (decltype(a->user_rank))sym("ncclCommUserRank");
   a->cu_device = (decltype(a->cu_device))sym("ncclCommCuDevice");
   a->all_gather = (decltype(a->all_gather))sym("ncclAllGather");
+  a->all_reduce = (decltype(a->all_reduce))sym("ncclAllReduce");
   a->error_string = (decltype(a->error_string))sym("ncclGetErrorString");
   a->async_error = (decltype(a->async_error))sym("ncclCommGetAsyncError");
   g_api = a;
@@ -79,11 +82,24 @@ void check(ncclResult_t r, const char* what) {
 
 }  // namespace
 
+// Two output buffers of every rank mapped into every rank (CUDA IPC), used
+// alternately by successive gathered contractions: a contraction's kernel
+// writes each output tile it computes into the current buffer of every rank.
+struct SymBuffers {
+  size_t bytes = 0;
+  void* local[2] = {nullptr, nullptr};
+  void* peer[2][kMaxSymRanks] = {};  // rank r's buffer b as mapped here (own rank: local)
+  int next = 0;
+};
+
 struct Comm {
   ncclComm_t nc = nullptr;
   int rank = 0, nranks = 1, device = -1;
   bool owned = false;         // created here (destroyed on release)
   cudaStream_t stream = nullptr;  // the communicator's transfer stream
+  int* dflag = nullptr;       // device word of the barrier (an all-reduce of one int)
+  SymBuffers sym;
+  bool sym_failed = false;    // mapping failed on some rank: gathers use the all-gather path
 };
 
 int comm_rank(const Comm& c) { return c.rank; }
@@ -101,6 +117,108 @@ void comm_allgather(Comm& c, void* buf, size_t doubles_per_rank, cudaStream_t af
   double* base = (double*)buf;
   check(a.all_gather(base + (size_t)c.rank * doubles_per_rank, base, doubles_per_rank, ncclDouble, c.nc, c.stream),
         "ncclAllGather");
+}
+
+void comm_barrier(Comm& c, cudaStream_t after, cudaStream_t then) {
+  const NcclApi& a = api();
+  cudaEvent_t ev;
+  NDT_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+  NDT_CUDA(cudaEventRecord(ev, after));
+  NDT_CUDA(cudaStreamWaitEvent(c.stream, ev, 0));
+  check(a.all_reduce(c.dflag, c.dflag, 1, ncclInt32, ncclMax, c.nc, c.stream), "ncclAllReduce");
+  NDT_CUDA(cudaEventRecord(ev, c.stream));
+  NDT_CUDA(cudaStreamWaitEvent(then, ev, 0));
+  cudaEventDestroy(ev);
+}
+
+namespace {
+
+void sym_release(Comm& c) {
+  for (int b = 0; b < 2; b++) {
+    for (int r = 0; r < c.nranks && r < kMaxSymRanks; r++)
+      if (r != c.rank && c.sym.peer[b][r]) cudaIpcCloseMemHandle(c.sym.peer[b][r]);
+    if (c.sym.local[b]) cudaFree(c.sym.local[b]);
+    c.sym.local[b] = nullptr;
+    for (int r = 0; r < kMaxSymRanks; r++) c.sym.peer[b][r] = nullptr;
+  }
+  c.sym.bytes = 0;
+}
+
+}  // namespace
+
+bool comm_symmetric(Comm& c, size_t bytes, cudaStream_t s, void** mine, void** peers) {
+  if (c.nranks > kMaxSymRanks || c.sym_failed) return false;
+  if (bytes > c.sym.bytes) {
+    // Collective (every rank asks for the same size at the same call).  The
+    // barrier and the waits make sure no rank's earlier kernel still writes
+    // into the buffers being replaced.
+    const NcclApi& a = api();
+    comm_barrier(c, s, s);
+    NDT_CUDA(cudaStreamSynchronize(c.stream));
+    NDT_CUDA(cudaStreamSynchronize(s));
+    sym_release(c);
+    const size_t want = (bytes + (2u << 20) - 1) / (2u << 20) * (2u << 20);
+    int ok = 1;
+    cudaIpcMemHandle_t h[2];
+    for (int b = 0; b < 2 && ok; b++) {
+      if (cudaMalloc(&c.sym.local[b], want) != cudaSuccess || cudaIpcGetMemHandle(&h[b], c.sym.local[b]) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+      }
+    }
+    // every rank allocated and exported its buffers?  (No handle is opened
+    // unless all of them exist.)
+    auto all_ranks = [&](int flag) {
+      NDT_CUDA(cudaMemcpy(c.dflag, &flag, sizeof(int), cudaMemcpyHostToDevice));
+      check(a.all_reduce(c.dflag, c.dflag, 1, ncclInt32, ncclSum, c.nc, c.stream), "ncclAllReduce");
+      NDT_CUDA(cudaStreamSynchronize(c.stream));
+      int total = 0;
+      NDT_CUDA(cudaMemcpy(&total, c.dflag, sizeof(int), cudaMemcpyDeviceToHost));
+      return total == c.nranks;
+    };
+    if (!all_ranks(ok)) {
+      sym_release(c);
+      c.sym_failed = true;
+      return false;
+    }
+    // every rank's two handles, then whether every rank mapped every buffer
+    const size_t hb = sizeof(cudaIpcMemHandle_t) * 2;
+    std::vector<char> all((size_t)c.nranks * hb);
+    char* dbuf = nullptr;
+    NDT_CUDA(cudaMalloc(&dbuf, all.size()));
+    NDT_CUDA(cudaMemcpy(dbuf + (size_t)c.rank * hb, h, hb, cudaMemcpyHostToDevice));
+    check(a.all_gather(dbuf + (size_t)c.rank * hb, dbuf, hb, ncclChar, c.nc, c.stream), "ncclAllGather");
+    NDT_CUDA(cudaStreamSynchronize(c.stream));
+    NDT_CUDA(cudaMemcpy(all.data(), dbuf, all.size(), cudaMemcpyDeviceToHost));
+    cudaFree(dbuf);
+    for (int r = 0; r < c.nranks && ok; r++) {
+      for (int b = 0; b < 2 && ok; b++) {
+        if (r == c.rank) {
+          c.sym.peer[b][r] = c.sym.local[b];
+          continue;
+        }
+        cudaIpcMemHandle_t ph;
+        memcpy(&ph, all.data() + (size_t)r * hb + b * sizeof(cudaIpcMemHandle_t), sizeof(ph));
+        if (cudaIpcOpenMemHandle(&c.sym.peer[b][r], ph, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+          cudaGetLastError();
+          c.sym.peer[b][r] = nullptr;
+          ok = 0;
+        }
+      }
+    }
+    if (!all_ranks(ok)) {
+      sym_release(c);
+      c.sym_failed = true;
+      return false;
+    }
+    c.sym.bytes = want;
+    c.sym.next = 0;
+  }
+  const int b = c.sym.next;
+  c.sym.next ^= 1;
+  *mine = c.sym.local[b];
+  for (int r = 0; r < c.nranks; r++) peers[r] = c.sym.peer[b][r];
+  return true;
 }
 
 void comm_join(Comm& c, cudaStream_t s) {
@@ -138,6 +256,8 @@ int ndt_b200_comm_unique_id(unsigned char* id) {
 
 static ndt_comm* finish_comm(Comm c, int* status) {
   NDT_CUDA(cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking));
+  NDT_CUDA(cudaMalloc(&c.dflag, sizeof(int)));
+  NDT_CUDA(cudaMemset(c.dflag, 0, sizeof(int)));
   *status = NDT_SUCCESS;
   return new ndt_comm{c};
 }
@@ -206,6 +326,9 @@ void ndt_b200_comm_release(ndt_comm* c) {
     cudaStreamSynchronize(c->c.stream);
     cudaStreamDestroy(c->c.stream);
   }
+  cudaDeviceSynchronize();  // no kernel of this process still writes into the mapped buffers
+  sym_release(c->c);
+  if (c->c.dflag) cudaFree(c->c.dflag);
   if (c->c.owned && c->c.nc && g_api) g_api->destroy(c->c.nc);
   delete c;
 }

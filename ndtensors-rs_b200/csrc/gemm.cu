@@ -40,6 +40,8 @@
 namespace ndt {
 namespace {
 
+constexpr int kMaxPeerCopies = 7;
+
 struct KArgs {
   const void* A;
   const void* B;
@@ -57,6 +59,10 @@ struct KArgs {
   int ntiles;          // grouped mode: entries of `tiles`
   int* counter;        // grouped mode: [tiles reserved, CTAs done], zero at launch
   int sm_reserve;      // grouped mode: SMs to leave free of persistent CTAs
+  // grouped mode: further copies of C (other ranks' output buffers mapped
+  // into this process) that every tile is also written to
+  int npeers;
+  char* peer_c[kMaxPeerCopies];
 };
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
@@ -649,9 +655,11 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   int c_i = 0, csteps = 0;
   int64_t cm = 0, cn = 0, c_off = 0, cm0 = 0, cn0 = 0;
   int mrows = 0, ncols = 0;  // rows / columns of this warp's tile that lie in the block
-  // C tile (+)= acc for the compute tile; clears acc.
+  // C tile (+)= acc for the compute tile (and = acc into every peer copy of
+  // C); clears acc.
   auto epilogue = [&]() {
     char* Cb = (char*)args.C + c_off * ES;
+    const int np = args.npeers;
 #pragma unroll
     for (int i = 0; i < MT; i++)
 #pragma unroll
@@ -671,11 +679,14 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
                 v.y += o.y;
               }
               *p = v;
+              for (int r = 0; r < np; r++)
+                reinterpret_cast<double2*>(args.peer_c[r] + c_off * ES)[row + col * cm] = v;
             } else {
               double* p = reinterpret_cast<double*>(Cb) + (row + col * cm);
               double v = acc[i][j][q];
               if (args.accumulate) v += *p;
               *p = v;
+              for (int r = 0; r < np; r++) reinterpret_cast<double*>(args.peer_c[r] + c_off * ES)[row + col * cm] = v;
             }
           }
 #pragma unroll
@@ -857,6 +868,9 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     }
   }
   cp_wait<0>();
+  // Stores into other GPUs' copies of C are visible system-wide before the
+  // kernel completes.
+  if (args.npeers) __threadfence_system();
   // The last CTA to finish leaves the reservation counters at zero for the
   // next launch over the same table: every other CTA made its last
   // reservation before it counted itself done.
@@ -1132,7 +1146,8 @@ const GroupedPlan* plan_insert(PlanKey&& k, const GroupedPlan& p) {
 
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* kscale, cudaStream_t s, bool kscale_real, int sm_reserve) {
+                  const void* kscale, cudaStream_t s, bool kscale_real, int sm_reserve,
+                  const std::vector<void*>* peer_copies) {
   if (probs.empty()) return;
   const bool cplx = dt == DType::C128;
   const DeviceCtx& c = ctx();
@@ -1233,6 +1248,11 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   a.tiles = (const int4*)(d + plan->off_t);
   a.counter = (int*)(d + plan->off_c);
   a.sm_reserve = sm_reserve;
+  a.npeers = 0;
+  if (peer_copies) {
+    if (peer_copies->size() > (size_t)kMaxPeerCopies) throw Error(ErrKind::InvalidArgument, "too many copies of C");
+    for (void* p : *peer_copies) a.peer_c[a.npeers++] = (char*)p;
+  }
   a.probs = (const GroupedProblem*)d;
   a.segs = (const GroupedSegment*)(d + plan->off_s);
   a.kscale = kscale;

@@ -257,10 +257,13 @@ struct GroupedSegment {
   int64_t scale_off;     // offset into the k-scale vector, or -1
 };
 // sm_reserve: SMs left free of the launch's persistent CTAs (room for
-// transfer kernels that run beside it, e.g. NCCL's).
+// transfer kernels that run beside it, e.g. NCCL's).  peer_copies (at most
+// 7): further buffers laid out like C (other GPUs' memory mapped into this
+// process) that every output tile is also stored to as it is computed.
 void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
-                  const void* kscale, cudaStream_t s, bool kscale_real = false, int sm_reserve = 0);
+                  const void* kscale, cudaStream_t s, bool kscale_real = false, int sm_reserve = 0,
+                  const std::vector<void*>* peer_copies = nullptr);
 
 // Block-sparse device helpers (blocksparse_kernels.cu).  A block table entry
 // describes one block: its extents, and for the dense side its start offset
