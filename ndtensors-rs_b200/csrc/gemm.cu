@@ -49,7 +49,6 @@ struct KArgs {
   // dense mode (tiles == nullptr)
   int64_t m, n, k, lda, ldb, ldc;
   int mtiles, ntiles_n;
-  int64_t kchunk;  // dense mode with a K split across a cluster: k range of each CTA
   // grouped mode
   const int4* tiles;  // x = problem, y = tile m index, z = tile n index
   const GroupedProblem* probs;
@@ -96,25 +95,6 @@ __device__ __forceinline__ double dneg(double x) {
   return __longlong_as_double(__double_as_longlong(x) ^ (long long)0x8000000000000000ULL);
 }
 
-// Thread block clusters (sm_90+): rank in the cluster, a barrier over the
-// cluster's CTAs, and a load from another CTA's shared memory.
-__device__ __forceinline__ unsigned cluster_rank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ double ld_cluster(const double* p, unsigned rank) {
-  const unsigned a = (unsigned)__cvta_generic_to_shared(p);
-  unsigned ra;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(ra) : "r"(a), "r"(rank));
-  double v;
-  asm volatile("ld.shared::cluster.f64 %0, [%1];\n" : "=d"(v) : "r"(ra) : "memory");
-  return v;
-}
-
 // Shared-memory pitch (in elements) of an operand tile.
 template <bool CPLX, bool KMAJOR, int MN, int BK>
 struct Pitch {
@@ -156,22 +136,12 @@ struct CopyPlan {
 // A and B (A . diag(s) . B) costs no pass of its own over A.  1: real scale
 // values (f64, or complex ones with zero imaginary parts: one multiply per
 // real component), 2: complex scale values (a complex multiply).
-// KS > 1 (f64): the K range is cut into KS pieces computed by the KS CTAs of
-// a thread block cluster (cluster rank = piece), each into its own registers;
-// the partial tiles meet in shared memory and every CTA sums a 1/KS slice of
-// the tile over the pieces in piece order (deterministic) through
-// distributed shared memory.  For GEMMs whose tiles leave the SMs' tensor
-// pipes unevenly loaded (the MPS merge: 256 tiles of 64 x 64 = 1024 warp
-// tiles on 592 SM sub-partitions, the busiest with 2 where the mean is 1.73),
-// KS = 4 makes 4096 quarter warp tiles: 7 on the busiest against 6.92.
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
-          int KS>
+          bool GROUPED, int SCALE>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(const __grid_constant__ KArgs args) {
   pdl_release();
-  pdl_wait();  // before the first global access (operands)
-  constexpr bool GROUPED = false;  // grouped work runs in dmma_grouped_kernel
-  constexpr int SCALE = 0;
-  static_assert(KS == 1 || (!CPLX && BN % KS == 0), "cluster K split: f64, BN a multiple of KS");
+  pdl_wait();  // before the first global access (tile tables, operands)
+  static_assert(SCALE == 0 || GROUPED, "k-scaling is a grouped-mode feature");
   using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM, SCALE>;
   constexpr int NTH = C::kThreads, MT = C::MT, NT = C::NT, ES = C::ES;
   constexpr int LDA = C::PA::value, LDB = C::PB::value;
@@ -194,7 +164,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
   const char* Bb = (const char*)args.B;
   if constexpr (!GROUPED) {
     // dense: rasterise with groups of 8 tile-rows for L2 reuse
-    int bid = blockIdx.x / KS;
+    int bid = blockIdx.x;
     const int GROUP = 8;
     int per_group = GROUP * args.ntiles_n;
     int grp = bid / per_group;
@@ -229,20 +199,12 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
   // Rows of the tile that exist in the matrix for the M / N side: fixed per tile.
   const int64_t a_mrem = m - m0, b_nrem = n - n0;
 
-  // this CTA's k range: all of k, or its cluster rank's piece
-  int64_t kbeg = 0, kend = args.k;
-  if constexpr (KS > 1) {
-    kbeg = (int64_t)cluster_rank() * args.kchunk;
-    kend = min(args.k, kbeg + args.kchunk);
-    if (kend < kbeg) kend = kbeg;
-  }
   // ---- load iterator over (segment, k0)
   int64_t seg = seg_begin, seg_end = seg_begin + seg_count;
   int64_t a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0, s_off = 0;
   auto load_seg = [&](int64_t s) {
     if constexpr (!GROUPED) {
-      kseg = kend;
-      k0 = kbeg;
+      kseg = args.k;
       lda = args.lda;
       ldb = args.ldb;
     } else {
@@ -257,7 +219,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
   };
   int total_steps = 0;
   if constexpr (!GROUPED) {
-    total_steps = (int)((kend - kbeg + BK - 1) / BK);
+    total_steps = (int)((args.k + BK - 1) / BK);
   } else {
     for (int64_t s = seg_begin; s < seg_end; s++) total_steps += (int)((args.segs[s].k + BK - 1) / BK);
   }
@@ -469,42 +431,6 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
     cs = (cs + 1 == STAGES) ? 0 : cs + 1;
   }
   cp_wait<0>();
-
-  if constexpr (KS > 1) {
-    // ---- partial tile -> own shared memory ([col][row], pitch BM + 2:
-    // conflict-free for the fragment layout), then each CTA sums columns
-    // [rank * BN / KS, (rank + 1) * BN / KS) over the KS pieces in order
-    constexpr int PP = BM + 2;
-    __syncthreads();  // every warp is done with the stages
-#pragma unroll
-    for (int i = 0; i < MT; i++)
-#pragma unroll
-      for (int j = 0; j < NT; j++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) {
-          const int row = wm0 + i * 16 + g + 8 * (q >> 1);
-          const int col = wn0 + j * 8 + 2 * t + (q & 1);
-          smem[col * PP + row] = acc[i][j][0 * 4 + q];
-        }
-    cluster_sync();  // every piece's partial is in place
-    const unsigned rk = cluster_rank();
-    constexpr int COLS = BN / KS;
-    double* Cd = reinterpret_cast<double*>(args.C);
-    for (int e = tid; e < BM * COLS; e += NTH) {
-      const int row = e % BM, col = (int)rk * COLS + e / BM;
-      double v = 0.0;
-#pragma unroll
-      for (int p = 0; p < KS; p++) v += ld_cluster(smem + col * PP + row, (unsigned)p);
-      const int64_t gr = m0 + row, gc = n0 + col;
-      if (gr < m && gc < n) {
-        double* p = Cd + (gr + gc * ldc);
-        if (args.accumulate) v += *p;
-        *p = v;
-      }
-    }
-    cluster_sync();  // the partials stay until every CTA has read them
-    return;
-  }
 
   // ---- epilogue: C[i + j*ldc] (+)= acc
   char* Cb = (char*)args.C + c_off * ES;
@@ -958,28 +884,13 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   }
 }
 
-template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, int KS>
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, bool GROUPED,
+          int SCALE>
 void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
-  using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, 0>;
-  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, KS>;
+  using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, SCALE>;
+  auto kern = dmma_gemm_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, GROUPED, SCALE>;
   ensure_dynamic_smem((const void*)kern, C::smem_bytes);
-  if constexpr (KS == 1) {
-    launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
-  } else {
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(grid * KS);
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::smem_bytes;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = KS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    NDT_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
-  }
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }
@@ -1016,13 +927,8 @@ void launch_grouped(const KArgs& a, cudaStream_t s) {
 
 template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC>
 void launch_cfg(const KArgs& a, int grid, cudaStream_t s) {
-  if (a.tiles == nullptr && a.kchunk > 0) {
-    if constexpr (!CPLX && BM == 64 && BN == 64)
-      launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, 4>(a, grid, s);
-    else
-      throw Error(ErrKind::Panic, "cluster K split requested for a tile class without it");
-  } else if (a.tiles == nullptr)
-    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, 1>(a, grid, s);
+  if (a.tiles == nullptr)
+    launch_mode<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, false, 0>(a, grid, s);
   else if (a.kscale == nullptr)
     launch_grouped<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, 0>(a, s);
   else if (!CPLX || a.kscale_real)
@@ -1124,20 +1030,6 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   for (int cl = 1; cl < nclasses(cplx); cl++)
     if (waves_eff(cl) > waves_eff(cls)) cls = cl;
   const int bm = tile_class(cplx, cls).bm, bn = tile_class(cplx, cls).bn;
-  // Cluster K split (f64, 64 x 64 tiles): FP64 MMA throughput belongs to the
-  // SM sub-partitions, and a 64 x 64 tile puts one 32 x 32 warp tile on each
-  // of them, so the busiest sub-partition carries ceil(4 tiles / parts) warp
-  // tiles.  When four K pieces per tile (reduced inside a 4-CTA cluster)
-  // balance that much better, and k leaves each piece at least one k-step,
-  // the dense launch runs as clusters.
-  int64_t kchunk = 0;
-  if (!cplx && cls == 0) {
-    const double parts = (double)c.sm_count * 4;
-    const double tiles = (double)((m + 63) / 64) * (double)((n + 63) / 64);
-    auto eff = [&](double units) { return units / (parts * std::ceil(units / parts)); };
-    const int64_t kc = ((k + 3) / 4 + 31) / 32 * 32;
-    if (k >= 4 * 32 && k <= 4096 && eff(tiles * 16) > eff(tiles * 4) + 0.05 && 3 * kc < k) kchunk = kc;
-  }
   // Split-K: when the grid leaves much of its last wave idle and k is long,
   // the k-range is cut into S pieces (multiples of 32, at least 16 k-steps of
   // 32 each) computed as S problems of one grouped launch into a workspace,
@@ -1149,7 +1041,7 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
     const double slots = (double)c.sm_count * tc.per_sm;
     auto fill = [&](int S) { return tiles * S / (std::ceil(tiles * S / slots) * slots) * (S > 1 ? 0.97 : 1.0); };
     int S = 1;
-    for (int cand = 2; cand <= 4 && allow_split_k && kchunk == 0; cand++)
+    for (int cand = 2; cand <= 4 && allow_split_k; cand++)
       if (k / cand >= 16 * 32 && fill(cand) > fill(S) + 0.02) S = cand;
     if (S > 1) {
       std::vector<GroupedProblem> probs(S);
@@ -1183,7 +1075,6 @@ void gemm(DType dt, int64_t m, int64_t n, int64_t k, GemmOperand A, GemmOperand 
   a.mtiles = (int)((m + bm - 1) / bm);
   a.ntiles_n = (int)((n + bn - 1) / bn);
   a.tiles = nullptr;
-  a.kchunk = kchunk;
   a.accumulate = accumulate ? 1 : 0;
   int grid = a.mtiles * a.ntiles_n;
   const bool vec = aligned16(A.ptr) && aligned16(B.ptr) && A.ld % 2 == 0 && B.ld % 2 == 0;
