@@ -174,9 +174,45 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       row_offsets(a, tile * kTileRows + r, xo, co);
     }
   };
-  auto tile_base = [&](int64_t tile, int64_t* xb, int64_t* cb) {
-    *xb = *cb = 0;
-    if (a.fast) row_offsets(a, tile * kTileRows, xb, cb);
+  // Fast mode: the X / C base offsets of consecutive tiles follow from one
+  // another without a division: the fastest row axis advances by a tile and
+  // carries into the slower ones when it wraps.
+  struct TileIt {
+    uint32_t dig[kMaxDims];
+    int64_t xb, cb;
+  };
+  auto it_init = [&](TileIt& it, int64_t tile) {
+    it.xb = it.cb = 0;
+    uint32_t r = (uint32_t)(tile * kTileRows);
+#pragma unroll
+    for (int d = 0; d < kMaxDims; d++) {
+      it.dig[d] = 0;
+      if (d < a.nd) {
+        uint32_t digit = r;
+        if (d + 1 < a.nd) {
+          const uint32_t q = r / a.ext[d];
+          digit = r - q * a.ext[d];
+          r = q;
+        }
+        it.dig[d] = digit;
+        it.xb += (int64_t)digit * a.xs[d];
+        it.cb += (int64_t)digit * a.cs[d];
+      }
+    }
+  };
+  auto it_next = [&](TileIt& it) {
+    it.dig[0] += kTileRows;
+    it.xb += kTileRows * a.xs[0];
+    it.cb += kTileRows * a.cs[0];
+#pragma unroll
+    for (int d = 0; d + 1 < kMaxDims; d++) {
+      if (d + 1 < a.nd && it.dig[d] == a.ext[d]) {
+        it.dig[d] = 0;
+        it.xb += a.xs[d + 1] - (int64_t)a.ext[d] * a.xs[d];
+        it.cb += a.cs[d + 1] - (int64_t)a.ext[d] * a.cs[d];
+        it.dig[d + 1] += 1;
+      }
+    }
   };
   // copy of tile `tile` into `stage`.  Pair mode (f64): thread tid brings
   // rows 2p, 2p+1 (p = tid % 128) for l = h, h + 2, ... (h = tid / 128) in
@@ -187,14 +223,13 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
     const int l = 2 * u + (tid >> 7);
     xkh[u] = l < a.k ? a.xk[l] : 0;
   }
-  auto issue = [&](int64_t tile, int stage) {
+  auto issue = [&](int64_t tile, int stage, int64_t xb, int64_t cb) {
     T* sbase = Xs + stage * STAGE;
     if (!CPLX && a.pair) {
       const int p = tid & 127, h = tid >> 7;
       const int64_t i = tile * kTileRows + 2 * p;
       if (i < a.rows) {
-        int64_t xb, cb, xo, co;
-        tile_base(tile, &xb, &cb);
+        int64_t xo, co;
         offs(tile, 2 * p, xb, cb, &xo, &co);
         const int bytes = i + 1 < a.rows ? 16 : 8;
         const T* src = X + xo;
@@ -206,8 +241,7 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       return;
     }
     if (tile * kTileRows + tid < a.rows) {
-      int64_t xb, cb, xo, co;
-      tile_base(tile, &xb, &cb);
+      int64_t xo, co;
       offs(tile, tid, xb, cb, &xo, &co);
       const T* src = X + xo;
       T* dst = sbase + tid;
@@ -216,11 +250,21 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
         if (l < a.k) cp_async<ES>(dst + l * kPitch, src + a.xk[l]);
     }
   };
-  const int64_t t0 = blockIdx.x, tstep = gridDim.x;
+  // Each CTA takes a contiguous run of tiles (consecutive tiles: one
+  // offset update each in fast mode).
+  const int64_t t0 = blockIdx.x * a.ntiles / gridDim.x, t1 = (blockIdx.x + 1) * a.ntiles / gridDim.x;
+  TileIt iti, itc;  // the next tile to issue, the tile being computed
+  if (a.fast) {
+    it_init(iti, t0);
+    itc = iti;
+  }
 #pragma unroll
   for (int s = 0; s < kStages - 1; s++) {
-    const int64_t tile = t0 + s * tstep;
-    if (tile < a.ntiles) issue(tile, s);
+    const int64_t tile = t0 + s;
+    if (tile < t1) {
+      issue(tile, s, a.fast ? iti.xb : 0, a.fast ? iti.cb : 0);
+      if (a.fast) it_next(iti);
+    }
     cp_commit();
   }
   for (int e = tid; e < kStages * kPitch; e += kThreads)
@@ -244,17 +288,19 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       }
 
   int stage = 0;
-  for (int64_t tile = t0; tile < a.ntiles; tile += tstep) {
+  for (int64_t tile = t0; tile < t1; tile++) {
     cp_wait<kStages - 2>();
     __syncthreads();  // tile landed for all threads; the stage refilled below is free
     {
-      const int64_t tn = tile + (kStages - 1) * tstep;
-      if (tn < a.ntiles) issue(tn, stage == 0 ? kStages - 1 : stage - 1);
+      const int64_t tn = tile + (kStages - 1);
+      if (tn < t1) {
+        issue(tn, stage == 0 ? kStages - 1 : stage - 1, a.fast ? iti.xb : 0, a.fast ? iti.cb : 0);
+        if (a.fast) it_next(iti);
+      }
       cp_commit();
     }
     const T* xs = Xs + stage * STAGE;
-    int64_t xb, cb;
-    tile_base(tile, &xb, &cb);
+    const int64_t xb = a.fast ? itc.xb : 0, cb = a.fast ? itc.cb : 0;
 #pragma unroll
     for (int mt = 0; mt < 2; mt++) {
       const int row0 = warp * 32 + mt * 16;
@@ -335,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       }
     }
     stage = stage + 1 == kStages ? 0 : stage + 1;
+    if (a.fast) it_next(itc);
   }
   asm volatile("cp.async.wait_all;\n" ::);
 }
