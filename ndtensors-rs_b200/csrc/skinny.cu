@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
   constexpr int kPitch = pitch<CPLX>();
   const int STAGE = (a.k + 1) * kPitch;
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  __shared__ int64_t s_cb[kStages];  // C base offset of the tile in each stage (fast mode)
   T* Xs = reinterpret_cast<T*>(smem_raw);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
   }
   auto issue = [&](int64_t tile, int stage, int64_t xb, int64_t cb) {
     T* sbase = Xs + stage * STAGE;
+    if (tid == 0) s_cb[stage] = cb;  // read when the stage is computed, after a barrier
     if (!CPLX && a.pair) {
       const int p = tid & 127, h = tid >> 7;
       const int64_t i = tile * kTileRows + 2 * p;
@@ -253,11 +255,8 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
   // Each CTA takes a contiguous run of tiles (consecutive tiles: one
   // offset update each in fast mode).
   const int64_t t0 = blockIdx.x * a.ntiles / gridDim.x, t1 = (blockIdx.x + 1) * a.ntiles / gridDim.x;
-  TileIt iti, itc;  // the next tile to issue, the tile being computed
-  if (a.fast) {
-    it_init(iti, t0);
-    itc = iti;
-  }
+  TileIt iti;  // the next tile to issue
+  if (a.fast) it_init(iti, t0);
 #pragma unroll
   for (int s = 0; s < kStages - 1; s++) {
     const int64_t tile = t0 + s;
@@ -300,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       cp_commit();
     }
     const T* xs = Xs + stage * STAGE;
-    const int64_t xb = a.fast ? itc.xb : 0, cb = a.fast ? itc.cb : 0;
+    const int64_t xb = 0, cb = a.fast ? s_cb[stage] : 0;  // stores need C's offsets only
 #pragma unroll
     for (int mt = 0; mt < 2; mt++) {
       const int row0 = warp * 32 + mt * 16;
@@ -381,7 +380,6 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
       }
     }
     stage = stage + 1 == kStages ? 0 : stage + 1;
-    if (a.fast) it_next(itc);
   }
   asm volatile("cp.async.wait_all;\n" ::);
 }
