@@ -118,29 +118,53 @@ BlockSparseT make_bs(DType dt, const std::vector<std::vector<size_t>>& bsz,
   return t;
 }
 
-// Per-block permute of a packed tensor: block b (shape sh_b) goes to the
-// same offset in dst with axes reordered by perm.
+// Per-block permute of a packed tensor: block order[r] (shape sh) goes to
+// dst + dst_offs[r] with its axes reordered by perm.  Many small blocks go
+// in one launch (the block map kernel: each source element, in its block's
+// column-major order, lands at its offset in the permuted block); few or
+// large blocks go one tiled permute launch each.
 void permute_blocks(DType dt, const void* src, void* dst, const BlockSparseT& t, const std::vector<size_t>& perm,
                     const std::vector<size_t>& dst_offs, const std::vector<size_t>& order, cudaStream_t s) {
-  const size_t es = esize(dt);
-  for (size_t r = 0; r < order.size(); r++) {
-    size_t b = order[r];
-    std::vector<size_t> sh = t.block_shape(t.coords[b]);
-    std::vector<size_t> st = col_major_strides(sh);
-    GatherDesc g;
-    for (size_t i = 0; i < perm.size(); i++) {
-      g.shape.push_back(sh[perm[i]]);
-      g.src_strides.push_back((int64_t)st[perm[i]]);
+  if (t.total() == 0) return;
+  if (t.nnzb() <= 16 || t.total() / t.nnzb() >= (size_t)1 << 16) {
+    const size_t es = esize(dt);
+    for (size_t r = 0; r < order.size(); r++) {
+      const size_t b = order[r];
+      if (t.block_elems(t.coords[b]) == 0) continue;
+      const std::vector<size_t> sh = t.block_shape(t.coords[b]);
+      const std::vector<size_t> st = col_major_strides(sh);
+      GatherDesc g;
+      for (size_t i = 0; i < perm.size(); i++) {
+        g.shape.push_back(sh[perm[i]]);
+        g.src_strides.push_back((int64_t)st[perm[i]]);
+      }
+      const char* sp = (const char*)src + t.offs[b] * es;
+      char* dp = (char*)dst + dst_offs[r] * es;
+      if (g.shape.empty())
+        NDT_CUDA(cudaMemcpyAsync(dp, sp, es, cudaMemcpyDeviceToDevice, s));
+      else
+        gather(dt, sp, dp, g, s);
     }
-    const char* sp = (const char*)src + t.offs[b] * es;
-    char* dp = (char*)dst + dst_offs[r] * es;
-    if (t.block_elems(t.coords[b]) == 0) continue;
-    if (g.shape.empty()) {
-      NDT_CUDA(cudaMemcpyAsync(dp, sp, es, cudaMemcpyDeviceToDevice, s));
-    } else {
-      gather(dt, sp, dp, g, s);
-    }
+    return;
   }
+  std::vector<int64_t> dst_base(t.nnzb(), 0);
+  for (size_t r = 0; r < order.size(); r++) dst_base[order[r]] = (int64_t)dst_offs[r];
+  std::vector<int64_t> offs(t.nnzb());
+  std::vector<BsBlockDesc> desc(t.nnzb());
+  for (size_t b = 0; b < t.nnzb(); b++) {
+    offs[b] = (int64_t)t.offs[b];
+    const std::vector<size_t> sh = t.block_shape(t.coords[b]);
+    std::vector<size_t> psh(perm.size());
+    for (size_t i = 0; i < perm.size(); i++) psh[i] = sh[perm[i]];
+    const std::vector<size_t> ps = col_major_strides(psh);
+    BsBlockDesc& d = desc[b];
+    memset(&d, 0, sizeof(d));
+    d.ndim = (int32_t)sh.size();
+    for (size_t i = 0; i < sh.size(); i++) d.shape[i] = (int64_t)sh[i];
+    for (size_t i = 0; i < perm.size(); i++) d.dstride[perm[i]] = (int64_t)ps[i];
+    d.dense_base = dst_base[b];
+  }
+  bs_dense_map(dt, const_cast<void*>(src), dst, offs, desc, (int64_t)t.total(), true, s);
 }
 
 bool is_prefix_run(const std::vector<size_t>& v, size_t start) {

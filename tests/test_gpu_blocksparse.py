@@ -470,3 +470,25 @@ def test_from_device_blocks_sorts_and_packs(gpu, cplx):
     assert np.array_equal(t.to_numpy_data(), np.concatenate([blocks[i].astype(dt) for i in order]))
     with pytest.raises(ValueError):
         cls.from_device_blocks(sizes, coords[:1], [pos - 1], dbuf.data_ptr(), dbuf.numel() // width)
+
+
+def test_cfg4_permuted_labels_many_blocks_vs_oracle(gpu, oracle):
+    """U(1) rank-4 at 1/8 scale with A's labels in a non-natural order
+    (-1, 1, -2, 2): A's 489 blocks are permuted to [free, contracted] in one
+    launch before the grouped GEMM; checked against the oracle."""
+    (sa, ca, a), (sb, cb, b), _, lb = cfg4_tensors(scale=8)
+    # A's axes relabelled: axis 0 and 2 contracted, 1 and 3 free
+    la = [-1, 1, -2, 2]
+    lb2 = [-1, -2, 3, 4]
+    _check(gpu, oracle, (sa, ca, a), la, (sb, cb, b), lb2)
+
+
+def test_cfg4_permutedims_many_blocks_bit_exact(gpu, oracle):
+    (sa, ca, a), _, _, _ = cfg4_tensors(scale=8)
+    t = gpu.blocksparse.BlockSparseF64.from_blocks(sa, ca, a)
+    for perm in ([2, 0, 3, 1], [3, 2, 1, 0]):
+        st, ref = oracle.bs_permutedims(oracle.BlockSparse(sa, ca, a), perm)
+        assert st == 0
+        p = t.permutedims(perm)
+        assert p.coords == ref.coords and p.block_sizes == ref.block_sizes
+        assert np.array_equal(p.to_numpy_data(), ref.data)
