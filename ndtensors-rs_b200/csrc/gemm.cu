@@ -50,7 +50,7 @@ struct KArgs {
   int64_t m, n, k, lda, ldb, ldc;
   int mtiles, ntiles_n;
   // grouped mode
-  const int4* tiles;  // x = problem, y = tile m index, z = tile n index
+  const int4* tiles;  // x = problem, y = tile m index, z = tile n index, w = k-steps (at least 1)
   const GroupedProblem* probs;
   const GroupedSegment* segs;
   const void* kscale;  // grouped mode: per-k scale (segments' scale_off), or null
@@ -708,12 +708,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     const int64_t mr = cm - cm0 - wm0, nc = cn - cn0 - wn0;
     mrows = mr < 0 ? 0 : (mr > C::WM ? C::WM : (int)mr);
     ncols = nc < 0 ? 0 : (nc > C::WN ? C::WN : (int)nc);
-    csteps = 0;
-    for (int64_t sidx = pr.seg_begin; sidx < pr.seg_begin + pr.seg_count; sidx++) {
-      const int64_t kk = args.segs[sidx].k;
-      if (kk > 0) csteps += (int)((kk + BK - 1) / BK);
-    }
-    if (csteps == 0) csteps = 1;
+    csteps = td.w;  // the tile's k-steps (at least 1), counted when the table was built
     return true;
   };
 
@@ -1168,7 +1163,8 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
       for (int64_t q = pr.seg_begin; q < pr.seg_begin + pr.seg_count; q++) ktot += (segs[q].k + bk - 1) / bk;
       int64_t mt = (pr.m + bm - 1) / bm, nt = (pr.n + bn - 1) / bn;
       for (int64_t i = 0; i < mt; i++)
-        for (int64_t j = 0; j < nt; j++) w.push_back({ktot, make_int4((int)p, (int)i, (int)j, 0)});
+        for (int64_t j = 0; j < nt; j++)
+          w.push_back({ktot, make_int4((int)p, (int)i, (int)j, (int)std::max<int64_t>(ktot, 1))});
     }
     std::stable_sort(w.begin(), w.end(), [](const auto& x, const auto& y) { return x.first > y.first; });
     tiles.resize(w.size());
