@@ -662,7 +662,8 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   const bool kreal = P->has_td && td->real;
   void* mine = nullptr;
   std::vector<void*> peers(kMaxSymRanks, nullptr);
-  if (gcomm && nranks > 1 && comm_symmetric(*gcomm, C.total() * es, s, &mine, peers.data())) {
+  const bool direct = gcomm && nranks > 1 && comm_symmetric(*gcomm, C.total() * es, s, &mine, peers.data());
+  if (direct) {
     // One launch computes this rank's output blocks and stores every tile
     // into this rank's mapped buffer and into every other rank's, over
     // NVLink, as it is computed (no separate transfer); a barrier over the
@@ -675,20 +676,22 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
                    0, &others);
     comm_barrier(*gcomm, s, s);
     NDT_CUDA(cudaMemcpyAsync(Cu, mine, C.total() * es, cudaMemcpyDeviceToDevice, s));
-    gcomm = nullptr;  // done: no staged launches below
-  }
-  void* stage = gcomm ? dev_alloc(P->stage_total * es, dev) : nullptr;
-  for (const PlannedLaunch& L : P->launches) {
-    if (!gcomm && mine) break;
-    if (!L.probs.empty())
-      grouped_gemm(A.dt, Ad, Bd, gcomm ? stage : Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
-                   gcomm && nranks > 1 ? kGatherSmReserve : 0);
-    if (gcomm) comm_allgather(*gcomm, (char*)stage + L.stage_off * es, L.pad * (es / 8), s);
-  }
-  if (gcomm) {
+  } else if (gcomm) {
+    // Staged: each chunk into this rank's slots of a staging buffer, an
+    // in-place NCCL all-gather per chunk, one copy into the sorted output.
+    void* stage = dev_alloc(P->stage_total * es, dev);
+    for (const PlannedLaunch& L : P->launches) {
+      if (!L.probs.empty())
+        grouped_gemm(A.dt, Ad, Bd, stage, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
+                     nranks > 1 ? kGatherSmReserve : 0);
+      comm_allgather(*gcomm, (char*)stage + L.stage_off * es, L.pad * (es / 8), s);
+    }
     comm_join(*gcomm, s);
     copy_segments(stage, Cu, P->copy_src, P->copy_dst, P->copy_bytes, s);
     dev_free(stage, dev);
+  } else {
+    for (const PlannedLaunch& L : P->launches)
+      if (!L.probs.empty()) grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal);
   }
   if (P->permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,
