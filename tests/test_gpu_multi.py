@@ -1,20 +1,23 @@
-"""Sharded block-sparse contraction on 2 GPUs over NCCL.
+"""Sharded block-sparse contraction on 2 to 8 GPUs over NCCL.
 
 Each rank computes its cost-balanced share of the output blocks
 (contract_shard, contract_through_diag) and the shards are gathered in HBM
 by the library (allgather over the library's NCCL communicator: one in-place
 all-gather, one copy kernel into the sorted output).  The gathered
 contractions of the C ABI (contract_gathered, contract_through_diag_gathered:
-compute and gather chunk by chunk) are checked the same way, and the c128
+each tile stored into every rank's mapped buffer as it is computed, or chunk
+by chunk over NCCL when the buffers cannot be mapped) are checked the same way, and the c128
 chain at bond 8192 block by block against the CPU block reference.  The
 gathered tensor must equal the unsharded contraction on one GPU (relative
-error 1e-12).  Runs as two spawned processes, one per GPU; skipped when fewer
-than two devices are visible.
+error 1e-12); every rank's gathered bytes must be identical.  Runs as one
+spawned process per visible GPU (at most 8); skipped when fewer than two
+devices are visible.
 """
 
 from __future__ import annotations
 
 import datetime
+import hashlib
 import os
 import socket
 import sys
@@ -98,12 +101,21 @@ def _worker(rank, world, port, q):
             g8 = bs.contract_through_diag_gathered(A8, [1, 2, -1], S8, [-1, -2], B8, [-2, 3, 4], comm)
         _, c8, o8 = g8._structure()
         d8 = g8.to_numpy_data()
-        ends = list(o8[1:]) + [len(d8)]
-        got = {tuple(int(x) for x in c): d8[o:e] for c, o, e in zip(c8, o8, ends)}
-        ref = reference_blocks(Ah, Bh, 2, 1, list(got), kscale=np.asarray(Sh[2]))
-        err = max(rel_fro(got[c], ref[c]) for c in ref)
-        results.append((f"cfg5 bond 8192 gathered vs CPU reference (max block err {err:.1e})",
-                        bool(err <= 1e-12 and len(got) == 128), -1, 128))
+        # every rank holds the same bytes (each block is computed by one rank
+        # and stored to all); rank 0 checks them against the CPU reference
+        digest = hashlib.sha256(np.ascontiguousarray(d8).tobytes()).hexdigest()
+        digests = [None] * world
+        dist.all_gather_object(digests, digest)
+        results.append(("cfg5 bond 8192 gathered bytes identical on every rank",
+                        all(d == digests[0] for d in digests), -1, 128))
+        if rank == 0:
+            ends = list(o8[1:]) + [len(d8)]
+            got = {tuple(int(x) for x in c): d8[o:e] for c, o, e in zip(c8, o8, ends)}
+            ref = reference_blocks(Ah, Bh, 2, 1, list(got), kscale=np.asarray(Sh[2]))
+            err = max(rel_fro(got[c], ref[c]) for c in ref)
+            results.append((f"cfg5 bond 8192 gathered vs CPU reference (max block err {err:.1e})",
+                            bool(err <= 1e-12 and len(got) == 128), -1, 128))
+        dist.barrier()
         del comm
         bs.Comm._by_group.clear()
         q.put((rank, results, None))
@@ -113,12 +125,14 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_sharded_contract_allgather_nccl_2gpu(gpu):
+def test_sharded_contract_allgather_nccl_multi_gpu(gpu):
+    """Every visible GPU (2 to 8) as one rank."""
     import multiprocessing as mp
 
     import torch
 
-    if torch.cuda.device_count() < 2:
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
         pytest.skip("needs two visible GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -126,10 +140,10 @@ def test_sharded_contract_allgather_nccl_2gpu(gpu):
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
-    out = [q.get(timeout=300) for _ in ps]
+    out = [q.get(timeout=600) for _ in ps]
     for p in ps:
         p.join(timeout=60)
     for rank, results, err in out:
