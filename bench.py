@@ -14,7 +14,7 @@ batched and complex128 permutes of the same 16^6 shape, the dense f64 MPS
 two-site merge A[256,4,256] x B[256,4,256] -> C[256,4,4,256], a 4096^3 GEMM,
 the DMRG environment chain at bond 1024 (per step), and the block-sparse
 U(1) rank-4 (half scale) and c128 two-site MPS contractions (sharded across
-ranks with --gpus N > 1, plus the NCCL gather).  At one GPU each contraction
+ranks with --gpus N > 1, plus the gathered output on every rank).  At one GPU each contraction
 also carries a CPU baseline: the reference's TTGT / per-pair algorithm with
 MKL (through torch) standing in for faer's GEMM, at one thread and at all
 host threads.
@@ -913,7 +913,9 @@ def run_blocksparse(args, torch, ndt, world, rank, pg):
         out.append({"cfg": "c5 c128 MPS+gather", "value": flops5 / (msg * 1e-3) / 1e12, "unit": "TFLOP/s",
                     "ms": msg, "n_gpus": world, "scaling": "strong", "parity": parg,
                     "gather": "gathered in the library (ndt_blocksparse_c64_contract_through_diag_gathered): "
-                              "an NCCL all-gather per chunk behind the next chunk's compute, one copy into the sorted output",
+                              "the grouped kernel's epilogue stores each tile into every rank's IPC-mapped buffer "
+                              "over NVLink, one NCCL barrier, one copy into the result (NCCL all-gather per chunk "
+                              "when the buffers cannot be mapped)",
                     "workload": "block-sparse c128 two-site MPS, sharded + gathered on every rank"})
         del rg
     if world >= 4:
