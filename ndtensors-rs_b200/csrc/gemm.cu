@@ -31,6 +31,7 @@
 #include <map>
 #include <mutex>
 #include <queue>
+#include <tuple>
 #include <type_traits>
 #include <unordered_map>
 #include <vector>
@@ -82,6 +83,23 @@ __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Bulk (TMA engine) copy of `bytes` (a multiple of 16, both addresses
+// 16-byte aligned) from this CTA's shared memory to global memory, which may
+// be another GPU's buffer mapped into this process: the engine reads the
+// shared memory and sends the data while the issuing warp goes on.
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, unsigned bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;\n" ::"l"(gdst),
+               "r"((unsigned)__cvta_generic_to_shared(ssrc)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// this thread's bulk copies have read their shared-memory source
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+// this thread's bulk copies are complete (their writes performed)
+__device__ __forceinline__ void bulk_wait_done() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+// this thread's shared-memory writes are visible to later bulk copies
+__device__ __forceinline__ void fence_shared_to_bulk() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+
 __device__ __forceinline__ void dmma(double& c0, double& c1, double& c2, double& c3, const double (&a)[4],
                                      const double (&b)[2]) {
   asm volatile(
@@ -117,6 +135,10 @@ struct Cfg {
   // SCALE: each stage also holds the BK scale values of its k range
   static constexpr int stage_elems = PA::elems + PB::elems + (SCALE ? BK : 0);
   static constexpr size_t smem_bytes = (size_t)STAGES * stage_elems * ES;
+  // complex grouped launches with peer copies of C: per warp, 8 columns of
+  // its tile (pitch WM + 1 elements) staged for the bulk copies to the peers
+  static constexpr int push_pitch = WM + 1;
+  static constexpr size_t push_bytes = CPLX ? (size_t)(kThreads / 32) * 8 * push_pitch * ES : 0;
 };
 
 // Copy pattern of one operand tile: ROWS x CONT elements in shared memory
@@ -660,6 +682,56 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   auto epilogue = [&]() {
     char* Cb = (char*)args.C + c_off * ES;
     const int np = args.npeers;
+    if constexpr (CPLX) {
+      if (np > 0) {
+        // Each 8-column group of the warp tile is stored into C and staged in
+        // shared memory; bulk copies then send each staged column (the warp's
+        // rows of it, contiguous in C) to every peer copy.  The warp goes on
+        // to the next tile while the copies drain; it waits only before it
+        // overwrites the staging, until the copies have read it.
+        double2* stg = reinterpret_cast<double2*>(smem + C::smem_bytes / sizeof(double)) +
+                       (size_t)warp * 8 * C::push_pitch;
+        const int64_t r0 = cm0 + wm0;
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+          bulk_wait_read();
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < MT; i++)
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              const int rl = i * 16 + g + 8 * (q >> 1), cl = 2 * t + (q & 1);
+              const int64_t row = r0 + rl, col = cn0 + wn0 + j * 8 + cl;
+              const double x = acc[i][j][q], y = acc[i][j][4 + q], z = acc[i][j][8 + q];
+              double2 v = make_double2(x - y, z - x - y);
+              if (row < cm && col < cn) {
+                double2* p = reinterpret_cast<double2*>(Cb) + (row + col * cm);
+                if (args.accumulate) {
+                  const double2 o = *p;
+                  v.x += o.x;
+                  v.y += o.y;
+                }
+                *p = v;
+              }
+              stg[cl * C::push_pitch + rl] = v;
+#pragma unroll
+              for (int pl = 0; pl < PLANES; pl++) acc[i][j][4 * pl + q] = 0.0;
+            }
+          fence_shared_to_bulk();
+          __syncwarp();
+          if (mrows > 0)
+            for (int e = lane; e < 8 * np; e += 32) {
+              const int cl = e & 7;
+              const int64_t col = cn0 + wn0 + j * 8 + cl;
+              if (col < cn)
+                bulk_store(args.peer_c[e >> 3] + (c_off + r0 + col * cm) * ES, stg + cl * C::push_pitch,
+                           (unsigned)mrows * ES);
+            }
+          bulk_commit();
+        }
+        return;
+      }
+    }
 #pragma unroll
     for (int i = 0; i < MT; i++)
 #pragma unroll
@@ -863,9 +935,12 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     }
   }
   cp_wait<0>();
-  // Stores into other GPUs' copies of C are visible system-wide before the
-  // kernel completes.
-  if (args.npeers) __threadfence_system();
+  // Stores into other GPUs' copies of C (the bulk copies complete) are
+  // visible system-wide before the kernel completes.
+  if (args.npeers) {
+    if constexpr (CPLX) bulk_wait_done();
+    __threadfence_system();
+  }
   // The last CTA to finish leaves the reservation counters at zero for the
   // next launch over the same table: every other CTA made its last
   // reservation before it counted itself done.
@@ -894,15 +969,15 @@ void launch_mode(const KArgs& a, int grid, cudaStream_t s) {
 // dynamic shared memory (looked up once per device and kernel).
 int resident_per_sm(const void* kern, int threads, size_t smem) {
   static std::mutex mu;
-  static std::map<std::pair<int, const void*>, int> cache;
+  static std::map<std::tuple<int, const void*, size_t>, int> cache;
   const int dev = current_device();
   std::lock_guard<std::mutex> lk(mu);
-  auto it = cache.find({dev, kern});
+  auto it = cache.find({dev, kern, smem});
   if (it != cache.end()) return it->second;
   int nb = 0;
   NDT_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem));
   if (nb < 1) nb = 1;
-  cache[{dev, kern}] = nb;
+  cache[{dev, kern, smem}] = nb;
   return nb;
 }
 
@@ -911,11 +986,13 @@ template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, 
 void launch_grouped(const KArgs& a, cudaStream_t s) {
   using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, SCALE>;
   auto kern = dmma_grouped_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, SCALE>;
-  ensure_dynamic_smem((const void*)kern, C::smem_bytes);
-  const int per_sm = resident_per_sm((const void*)kern, C::kThreads, C::smem_bytes);
+  // complex launches with peer copies of C also stage their epilogue
+  const size_t smem = C::smem_bytes + (a.npeers ? C::push_bytes : 0);
+  ensure_dynamic_smem((const void*)kern, smem);
+  const int per_sm = resident_per_sm((const void*)kern, C::kThreads, smem);
   const int sms = std::max(1, ctx().sm_count - std::max(0, a.sm_reserve));
   const int grid = (int)std::min<int64_t>(a.ntiles, (int64_t)per_sm * sms);
-  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::smem_bytes, s, a);
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), smem, s, a);
   count_launch();
   NDT_CUDA(cudaGetLastError());
 }
