@@ -173,6 +173,43 @@ bool is_prefix_run(const std::vector<size_t>& v, size_t start) {
   return true;
 }
 
+// The GEMM index over `axes` (that order, the first fastest) of a block with
+// extents `ext` and strides `str`, merged into strided runs (extent-1 axes
+// dropped, an axis continuing the previous run joins it).  False when it
+// takes more than two runs.
+bool index_runs(const std::vector<size_t>& axes, const std::vector<int64_t>& ext, const std::vector<int64_t>& str,
+                IndexRuns* out) {
+  std::vector<std::pair<int64_t, int64_t>> runs;  // (extent, stride)
+  for (size_t a : axes) {
+    if (ext[a] == 1) continue;
+    if (!runs.empty() && runs.back().first * runs.back().second == str[a])
+      runs.back().first *= ext[a];
+    else
+      runs.push_back({ext[a], str[a]});
+  }
+  if (runs.size() > 2) return false;
+  out->pad = 0;
+  out->e0 = 0x7fffffffu;  // one run (or none): every index is below it
+  out->s0 = runs.empty() ? 0 : runs[0].second;
+  out->s1 = 0;
+  if (runs.size() == 2) {
+    out->e0 = (uint32_t)runs[0].first;
+    out->s1 = runs[1].second;
+  }
+  return true;
+}
+
+// Column-major strides of a block with extents `ext`.
+std::vector<int64_t> block_strides(const std::vector<int64_t>& ext) {
+  std::vector<int64_t> st(ext.size());
+  int64_t s = 1;
+  for (size_t i = 0; i < ext.size(); i++) {
+    st[i] = s;
+    s *= ext[i];
+  }
+  return st;
+}
+
 }  // namespace
 
 // contract_blocksparse (contract/blocksparse.rs:87-183).  With nranks > 1 only
@@ -219,6 +256,9 @@ constexpr int kGatherSmReserve = 0;
 struct PlannedLaunch {
   std::vector<GroupedProblem> probs;
   std::vector<GroupedSegment> segs;
+  // strided plans: the index runs of every problem and segment
+  std::vector<StridedProblem> sprobs;
+  std::vector<StridedSegment> ssegs;
   // gathered mode: this chunk's region of the staging buffer (elements):
   // rank r's blocks of the chunk, packed, at stage_off + r * pad
   size_t stage_off = 0, pad = 0;
@@ -229,6 +269,9 @@ struct ContractPlan {
   bool a_kmajor = false, b_kmajor = true;
   bool pack_a = false, pack_b = false;  // operand blocks permuted to [free, contracted] first
   std::vector<size_t> perm_a, perm_b;
+  // the GEMM reads A and B and writes C through index runs (no pack, no
+  // output permute) instead of packing and permuting
+  bool strided = false;
   bool permute_c = false;
   std::vector<size_t> perm_c;
   bool has_td = false;
@@ -499,6 +542,74 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
       P->pack_b = true;
       P->b_kmajor = true;
     }
+    // Strided plan: instead of packing an operand or permuting the output,
+    // the GEMM addresses every block through its index runs, when each GEMM
+    // index of every block takes at most two runs and every block has fewer
+    // than 2^31 elements (no k-scale), and when that is not slower: complex
+    // tiles lose nothing measurable to the one-element copies (B200, the c128
+    // MPS chain with A's axes permuted: 31.4 TFLOP/s either way), f64 tiles
+    // about 8% (U(1) rank-4 half scale with A's labels (-1, 1, -2, 2): 27.6
+    // TFLOP/s against 29.6 with A packed first), so f64 takes the strided
+    // path while 8% of its GEMM time (at 30 TFLOP/s) stays below the passes
+    // it saves (each a read and a write at 6 TB/s, plus 5 us).
+    const bool permute_out = P->permute_c;  // the stored C layout, for the runs
+    auto seg_runs = [&](size_t a, size_t b, StridedSegment* ss) -> bool {
+      std::vector<int64_t> ea(na), eb(nb);
+      int64_t ta = 1, tb = 1;
+      for (size_t i = 0; i < na; i++) ta *= (ea[i] = (int64_t)A.bsz[i][A.coords[a][i]]);
+      for (size_t j = 0; j < nb; j++) tb *= (eb[j] = (int64_t)B.bsz[j][B.coords[b][j]]);
+      if (ta >= ((int64_t)1 << 31) || tb >= ((int64_t)1 << 31)) return false;
+      const std::vector<int64_t> sa = block_strides(ea), sb = block_strides(eb);
+      return index_runs(ua, ea, sa, &ss->am) && index_runs(pa, ea, sa, &ss->ak) && index_runs(pb, eb, sb, &ss->bk) &&
+             index_runs(ub, eb, sb, &ss->bn);
+    };
+    auto prob_runs = [&](size_t ob, StridedProblem* sp) -> bool {
+      // C's blocks hold [A free..., B free...] in label-sorted axis order:
+      // axis p of the stored block is unsorted axis perm_c[p]
+      const std::vector<size_t> sh = C.block_shape(C.coords[ob]);
+      std::vector<int64_t> ext(sh.size()), str(sh.size());
+      int64_t st = 1;
+      for (size_t p = 0; p < sh.size(); p++) {
+        const size_t u = permute_out ? perm_c[p] : p;
+        ext[u] = (int64_t)sh[u];
+        str[u] = st;
+        st *= (int64_t)sh[u];
+      }
+      if (st >= ((int64_t)1 << 31)) return false;
+      std::vector<size_t> mi, ni;
+      for (size_t i = 0; i < ua.size(); i++) mi.push_back(i);
+      for (size_t j = 0; j < ub.size(); j++) ni.push_back(ua.size() + j);
+      return index_runs(mi, ext, str, &sp->cm) && index_runs(ni, ext, str, &sp->cn);
+    };
+    if ((P->pack_a || P->pack_b || P->permute_c) && td_pos == SIZE_MAX) {
+      bool ok = true;
+      double flops = 0;
+      for (size_t ob = 0; ok && ob < C.nnzb(); ob++) {
+        StridedProblem sp{};
+        ok = prob_runs(ob, &sp);
+        for (auto& p2 : contrib[C.coords[ob]]) {
+          StridedSegment ss{};
+          if (!ok || !(ok = seg_runs(p2.first, p2.second, &ss))) break;
+          double m = 1, n = 1, k = 1;
+          for (size_t i : ua) m *= (double)A.bsz[i][A.coords[p2.first][i]];
+          for (size_t j : ub) n *= (double)B.bsz[j][B.coords[p2.second][j]];
+          for (size_t i : pa) k *= (double)A.bsz[i][A.coords[p2.first][i]];
+          flops += 2 * m * n * k;
+        }
+      }
+      if (ok && A.dt != DType::C128) {
+        const double es = (double)esize(A.dt);
+        double saved = 0;
+        if (P->pack_a) saved += 2 * (double)A.total() * es / 6e12 + 5e-6;
+        if (P->pack_b) saved += 2 * (double)B.total() * es / 6e12 + 5e-6;
+        if (P->permute_c) saved += 2 * (double)C.total() * es / 6e12 + 5e-6;
+        ok = 0.08 * flops / 30e12 <= saved;
+      }
+      if (ok) {
+        P->strided = true;
+        P->pack_a = P->pack_b = P->permute_c = false;
+      }
+    }
     // device tables: one problem per output block, one segment per pair
     auto make_table = [&](const std::vector<size_t>& obs, PlannedLaunch& L) {
       for (size_t ob : obs) {
@@ -523,8 +634,16 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
           sg.ldb = P->b_kmajor ? k : n;
           sg.scale_off = td_pos != SIZE_MAX ? td->qmap.at(A.coords[p2.first][td->a_axis]).second : -1;
           L.segs.push_back(sg);
+          if (P->strided) {
+            L.ssegs.emplace_back();
+            seg_runs(p2.first, p2.second, &L.ssegs.back());
+          }
         }
         L.probs.push_back(pr);
+        if (P->strided) {
+          L.sprobs.emplace_back();
+          prob_runs(ob, &L.sprobs.back());
+        }
       }
     };
     if (!gathered) {
@@ -660,6 +779,9 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   void* Cu = P->permute_c ? dev_alloc(C.total() * es, dev) : Cd;
   const void* kscale = P->has_td ? td->sdata : nullptr;
   const bool kreal = P->has_td && td->real;
+  // the index runs of a launch's table (strided plans only)
+  auto sruns = [&](const PlannedLaunch& L) { return P->strided ? &L.sprobs : nullptr; };
+  auto sruns_seg = [&](const PlannedLaunch& L) { return P->strided ? &L.ssegs : nullptr; };
   void* mine = nullptr;
   std::vector<void*> peers(kMaxSymRanks, nullptr);
   const bool direct = gcomm && nranks > 1 && comm_symmetric(*gcomm, C.total() * es, s, &mine, peers.data());
@@ -673,7 +795,7 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
       if (r != rank) others.push_back(peers[r]);
     if (!P->direct.probs.empty())
       grouped_gemm(A.dt, Ad, Bd, mine, P->a_kmajor, P->b_kmajor, P->direct.probs, P->direct.segs, kscale, s, kreal,
-                   0, &others);
+                   0, &others, sruns(P->direct), sruns_seg(P->direct));
     comm_barrier(*gcomm, s, s);
     NDT_CUDA(cudaMemcpyAsync(Cu, mine, C.total() * es, cudaMemcpyDeviceToDevice, s));
   } else if (gcomm) {
@@ -683,7 +805,7 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     for (const PlannedLaunch& L : P->launches) {
       if (!L.probs.empty())
         grouped_gemm(A.dt, Ad, Bd, stage, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal,
-                     nranks > 1 ? kGatherSmReserve : 0);
+                     nranks > 1 ? kGatherSmReserve : 0, nullptr, sruns(L), sruns_seg(L));
       comm_allgather(*gcomm, (char*)stage + L.stage_off * es, L.pad * (es / 8), s);
     }
     comm_join(*gcomm, s);
@@ -691,7 +813,9 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
     dev_free(stage, dev);
   } else {
     for (const PlannedLaunch& L : P->launches)
-      if (!L.probs.empty()) grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal);
+      if (!L.probs.empty())
+        grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, L.probs, L.segs, kscale, s, kreal, 0, nullptr,
+                     sruns(L), sruns_seg(L));
   }
   if (P->permute_c) {
     // contract_gemm returns each block in label-sorted order (same shape,

@@ -64,7 +64,16 @@ struct KArgs {
   // into this process) that every tile is also written to
   int npeers;
   char* peer_c[kMaxPeerCopies];
+  // grouped mode, strided operands: index runs per problem / segment
+  const StridedProblem* sprobs;
+  const StridedSegment* ssegs;
 };
+
+// offset of index x along its runs
+__device__ __forceinline__ int64_t run_off(const IndexRuns& r, uint32_t x) {
+  const uint32_t q = x / r.e0;
+  return (int64_t)(x - q * r.e0) * r.s0 + (int64_t)q * r.s1;
+}
 
 __device__ __forceinline__ void cp_async8(void* smem, const void* gmem, bool pred) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
@@ -508,10 +517,16 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
 // interior tiles take an unpredicated path.
 // A tile whose block has no contracted extent (all its segments empty) runs
 // one k-step of zeros and writes a zero tile.
+// STR (with AK, BKM, one-element copies and no k-scale): A, B and C are
+// addressed through each segment's and problem's index runs, so blocks whose
+// axes are not in GEMM order are read and written in place.  A thread's copy
+// rows keep one offset each per segment (set when the segment starts); its
+// contraction column adds one offset per stage.
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
-          int SCALE>
+          int SCALE, bool STR = false>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     dmma_grouped_kernel(const __grid_constant__ KArgs args) {
+  static_assert(!STR || (AK && BKM && !VEC && SCALE == 0), "strided operands: k-major staging, no k-scale");
   pdl_release();
   pdl_wait();  // before the first global access (tile tables, operands)
   using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM, SCALE>;
@@ -555,6 +570,8 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   int l_i = 0;
   int64_t l_m0 = 0, l_n0 = 0, a_mrem = 0, b_nrem = 0;
   int64_t seg = 0, seg_end = 0, a_off = 0, b_off = 0, kseg = 0, lda = 0, ldb = 0, k0 = 0, s_off = 0;
+  int32_t a_row[STR ? PlanA::IT : 1], b_row[STR ? PlanB::IT : 1];  // STR: copy-row offsets in the blocks
+  IndexRuns r_ak{}, r_bk{};
   auto load_seg = [&](int64_t sidx) {
     const GroupedSegment sd = args.segs[sidx];
     a_off = sd.a_off;
@@ -563,6 +580,17 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     lda = sd.lda;
     ldb = sd.ldb;
     s_off = sd.scale_off;
+    if constexpr (STR) {
+      const StridedSegment ss = args.ssegs[sidx];
+      r_ak = ss.ak;
+      r_bk = ss.bk;
+#pragma unroll
+      for (int it = 0; it < PlanA::IT; it++)
+        a_row[it] = (int32_t)run_off(ss.am, (uint32_t)(l_m0 + a_r + it * PlanA::RS));
+#pragma unroll
+      for (int it = 0; it < PlanB::IT; it++)
+        b_row[it] = (int32_t)run_off(ss.bn, (uint32_t)(l_n0 + b_r + it * PlanB::RS));
+    }
   };
   // Set the load side up on this CTA's l_i-th tile; false when it has no
   // tiles left.  A tile without a non-empty segment gets one null k-step
@@ -608,6 +636,35 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     double* Bs = As + (size_t)C::PA::elems * RPL;
     const int64_t krem = kseg - k0;  // k rows left in this segment
     if (tid == 0) s_kvalid[stage] = krem < BK ? (int)krem : BK;
+    if constexpr (STR) {
+      // A rows m (a_row), column k0 + a_c; B rows n (b_row), column k0 + b_c
+      const bool aok = a_c < krem, bok = b_c < krem;
+      const int64_t ka = aok ? a_off + run_off(r_ak, (uint32_t)(k0 + a_c)) : 0;
+      const int64_t kb = bok ? b_off + run_off(r_bk, (uint32_t)(k0 + b_c)) : 0;
+      double* da = As + ((size_t)a_r * LDA + a_c) * RPL;
+      double* db = Bs + ((size_t)b_r * LDB + b_c) * RPL;
+#pragma unroll
+      for (int it = 0; it < PlanA::IT; it++) {
+        const bool ok = aok && it * PlanA::RS < a_mrem - a_r;
+        const char* p = ok ? Ab + (ka + a_row[it]) * ES : Ab;
+        double* d = da + (size_t)it * PlanA::RS * LDA * RPL;
+        if constexpr (CPLX)
+          cp_async16n(d, p, ok ? 16 : 0);
+        else
+          cp_async8(d, p, ok);
+      }
+#pragma unroll
+      for (int it = 0; it < PlanB::IT; it++) {
+        const bool ok = bok && it * PlanB::RS < b_nrem - b_r;
+        const char* p = ok ? Bb + (kb + b_row[it]) * ES : Bb;
+        double* d = db + (size_t)it * PlanB::RS * LDB * RPL;
+        if constexpr (CPLX)
+          cp_async16n(d, p, ok ? 16 : 0);
+        else
+          cp_async8(d, p, ok);
+      }
+      return;
+    }
     {
       const int64_t cont_rem = AK ? krem - a_c : a_mrem - a_c;
       const int nv = cont_rem >= PW ? PW : (cont_rem > 0 ? (int)cont_rem : 0);
@@ -674,7 +731,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     for (int j = 0; j < NT; j++)
 #pragma unroll
       for (int q = 0; q < 4 * PLANES; q++) acc[i][j][q] = 0.0;
-  int c_i = 0, csteps = 0;
+  int c_i = 0, csteps = 0, c_prob = 0;
   int64_t cm = 0, cn = 0, c_off = 0, cm0 = 0, cn0 = 0;
   int mrows = 0, ncols = 0;  // rows / columns of this warp's tile that lie in the block
   // C tile (+)= acc for the compute tile (and = acc into every peer copy of
@@ -682,7 +739,20 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   auto epilogue = [&]() {
     char* Cb = (char*)args.C + c_off * ES;
     const int np = args.npeers;
-    if constexpr (CPLX) {
+    // STR: offsets of this thread's rows and columns in the C block
+    int64_t ro[STR ? MT : 1][2], co[STR ? NT : 1][2];
+    if constexpr (STR) {
+      const StridedProblem sp = args.sprobs[c_prob];
+#pragma unroll
+      for (int i = 0; i < MT; i++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) ro[i][h] = run_off(sp.cm, (uint32_t)(cm0 + wm0 + i * 16 + g + 8 * h));
+#pragma unroll
+      for (int j = 0; j < NT; j++)
+#pragma unroll
+        for (int b = 0; b < 2; b++) co[j][b] = run_off(sp.cn, (uint32_t)(cn0 + wn0 + j * 8 + 2 * t + b));
+    }
+    if constexpr (CPLX && !STR) {
       if (np > 0) {
         // Each 8-column group of the warp tile is stored into C and staged in
         // shared memory; bulk copies then send each staged column (the warp's
@@ -741,8 +811,13 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
           const int64_t row = cm0 + wm0 + i * 16 + g + 8 * (q >> 1);
           const int64_t col = cn0 + wn0 + j * 8 + 2 * t + (q & 1);
           if (row < cm && col < cn) {
+            int64_t e;
+            if constexpr (STR)
+              e = ro[i][q >> 1] + co[j][q & 1];
+            else
+              e = row + col * cm;
             if constexpr (CPLX) {
-              double2* p = reinterpret_cast<double2*>(Cb) + (row + col * cm);
+              double2* p = reinterpret_cast<double2*>(Cb) + e;
               const double x = acc[i][j][q], y = acc[i][j][4 + q], z = acc[i][j][8 + q];
               double2 v = make_double2(x - y, z - x - y);
               if (args.accumulate) {
@@ -751,14 +826,13 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
                 v.y += o.y;
               }
               *p = v;
-              for (int r = 0; r < np; r++)
-                reinterpret_cast<double2*>(args.peer_c[r] + c_off * ES)[row + col * cm] = v;
+              for (int r = 0; r < np; r++) reinterpret_cast<double2*>(args.peer_c[r] + c_off * ES)[e] = v;
             } else {
-              double* p = reinterpret_cast<double*>(Cb) + (row + col * cm);
+              double* p = reinterpret_cast<double*>(Cb) + e;
               double v = acc[i][j][q];
               if (args.accumulate) v += *p;
               *p = v;
-              for (int r = 0; r < np; r++) reinterpret_cast<double*>(args.peer_c[r] + c_off * ES)[row + col * cm] = v;
+              for (int r = 0; r < np; r++) reinterpret_cast<double*>(args.peer_c[r] + c_off * ES)[e] = v;
             }
           }
 #pragma unroll
@@ -772,6 +846,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     if (ti >= ntiles) return false;
     const int4 td = args.tiles[ti];
     const GroupedProblem pr = args.probs[td.x];
+    c_prob = td.x;
     cm = pr.m;
     cn = pr.n;
     c_off = pr.c_off;
@@ -938,7 +1013,7 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
   // Stores into other GPUs' copies of C (the bulk copies complete) are
   // visible system-wide before the kernel completes.
   if (args.npeers) {
-    if constexpr (CPLX) bulk_wait_done();
+    if constexpr (CPLX && !STR) bulk_wait_done();
     __threadfence_system();
   }
   // The last CTA to finish leaves the reservation counters at zero for the
@@ -982,12 +1057,13 @@ int resident_per_sm(const void* kern, int threads, size_t smem) {
 }
 
 // Grouped launch: the persistent kernel on min(tiles, resident CTAs) CTAs.
-template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, int SCALE>
+template <bool CPLX, int BM, int BN, int BK, int WMW, int WNW, int ST, bool AK, bool BKM, bool VEC, int SCALE,
+          bool STR = false>
 void launch_grouped(const KArgs& a, cudaStream_t s) {
   using C = Cfg<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, SCALE>;
-  auto kern = dmma_grouped_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, SCALE>;
+  auto kern = dmma_grouped_kernel<CPLX, BM, BN, BK, WMW, WNW, ST, AK, BKM, VEC, SCALE, STR>;
   // complex launches with peer copies of C also stage their epilogue
-  const size_t smem = C::smem_bytes + (a.npeers ? C::push_bytes : 0);
+  const size_t smem = C::smem_bytes + (a.npeers && !STR ? C::push_bytes : 0);
   ensure_dynamic_smem((const void*)kern, smem);
   const int per_sm = resident_per_sm((const void*)kern, C::kThreads, smem);
   const int sms = std::max(1, ctx().sm_count - std::max(0, a.sm_reserve));
@@ -1173,7 +1249,7 @@ struct PlanKeyHash {
 };
 struct GroupedPlan {
   char* d = nullptr;  // device table
-  size_t off_s = 0, off_t = 0, off_c = 0;
+  size_t off_s = 0, off_t = 0, off_c = 0, off_sp = 0, off_ss = 0;
   int cls = 0, ntiles = 0;
   cudaEvent_t last_use = nullptr;  // the last launch that read the table
   uint64_t tick = 0;
@@ -1219,9 +1295,13 @@ const GroupedPlan* plan_insert(PlanKey&& k, const GroupedPlan& p) {
 void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
                   const void* kscale, cudaStream_t s, bool kscale_real, int sm_reserve,
-                  const std::vector<void*>* peer_copies) {
+                  const std::vector<void*>* peer_copies, const std::vector<StridedProblem>* sprobs,
+                  const std::vector<StridedSegment>* ssegs) {
   if (probs.empty()) return;
   const bool cplx = dt == DType::C128;
+  const bool strided = sprobs != nullptr;
+  if (strided && (!ssegs || sprobs->size() != probs.size() || ssegs->size() != segs.size() || kscale))
+    throw Error(ErrKind::InvalidArgument, "strided grouped GEMM: one run set per problem and segment, no k-scale");
   const DeviceCtx& c = ctx();
   // Tile list: every (problem, tile) with its k length, heaviest first so
   // the tail of the launch is made of short tiles.  Each class is scored by
@@ -1271,18 +1351,27 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   // block structure), which then cost one launch and no host planning.
   PlanKey key;
   key.device = c.device;
-  key.flags = (cplx ? 1 : 0);
-  key.words.resize((probs.size() * sizeof(GroupedProblem) + segs.size() * sizeof(GroupedSegment)) / 8 + 1);
+  key.flags = (cplx ? 1 : 0) | (strided ? 2 : 0);
+  const size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment);
+  const size_t bsp = strided ? sprobs->size() * sizeof(StridedProblem) : 0;
+  const size_t bss = strided ? ssegs->size() * sizeof(StridedSegment) : 0;
+  key.words.resize((bp + bsg + bsp + bss) / 8 + 1);
   key.words[0] = (int64_t)probs.size();
-  memcpy(key.words.data() + 1, probs.data(), probs.size() * sizeof(GroupedProblem));
-  memcpy((char*)(key.words.data() + 1) + probs.size() * sizeof(GroupedProblem), segs.data(),
-         segs.size() * sizeof(GroupedSegment));
+  {
+    char* w = (char*)(key.words.data() + 1);
+    memcpy(w, probs.data(), bp);
+    memcpy(w + bp, segs.data(), bsg);
+    if (strided) {
+      memcpy(w + bp + bsg, sprobs->data(), bsp);
+      memcpy(w + bp + bsg + bsp, ssegs->data(), bss);
+    }
+  }
   const GroupedPlan* plan = plan_lookup(key);
   if (!plan) {
     std::vector<int4> tiles, cand;
     int cls = 0;
     double best = -1;
-    for (int cl = 0; cl < nclasses(cplx); cl++) {
+    for (int cl = 0; cl < (strided ? 1 : nclasses(cplx)); cl++) {  // strided: class 0 only
       double t;
       build(cl, cand, &t);
       if (best < 0 || t < best) {
@@ -1293,17 +1382,22 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
     }
     // Device-side tables: problems, segments, tiles, and the tile reservation
     // counters (zero; each launch leaves them zero for the next), one allocation.
-    size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment),
-           bt = tiles.size() * sizeof(int4);
+    const size_t bt = tiles.size() * sizeof(int4);
     GroupedPlan np;
     np.off_s = (bp + 255) / 256 * 256;
     np.off_t = np.off_s + (bsg + 255) / 256 * 256;
     np.off_c = np.off_t + (bt + 255) / 256 * 256;
-    const size_t total = np.off_c + 2 * sizeof(int);
-    std::vector<char> host(total);
+    np.off_sp = np.off_c + 256;
+    np.off_ss = np.off_sp + (bsp + 255) / 256 * 256;
+    const size_t total = np.off_ss + bss;
+    std::vector<char> host(total, 0);
     memcpy(host.data(), probs.data(), bp);
     memcpy(host.data() + np.off_s, segs.data(), bsg);
     memcpy(host.data() + np.off_t, tiles.data(), bt);
+    if (strided) {
+      memcpy(host.data() + np.off_sp, sprobs->data(), bsp);
+      memcpy(host.data() + np.off_ss, ssegs->data(), bss);
+    }
     np.d = (char*)pool_alloc(total, s);
     NDT_CUDA(cudaMemcpyAsync(np.d, host.data(), total, cudaMemcpyHostToDevice, s));
     // the copy reads pageable memory: it has been taken when the call returns
@@ -1328,6 +1422,8 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   }
   a.probs = (const GroupedProblem*)d;
   a.segs = (const GroupedSegment*)(d + plan->off_s);
+  a.sprobs = strided ? (const StridedProblem*)(d + plan->off_sp) : nullptr;
+  a.ssegs = strided ? (const StridedSegment*)(d + plan->off_ss) : nullptr;
   a.kscale = kscale;
   a.kscale_real = kscale_real ? 1 : 0;
   a.accumulate = 0;
@@ -1336,10 +1432,17 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   bool vec = aligned16(A) && aligned16(B);
   for (const GroupedSegment& sg : segs)
     vec = vec && sg.a_off % 2 == 0 && sg.b_off % 2 == 0 && sg.lda % 2 == 0 && sg.ldb % 2 == 0;
-  if (cplx)
+  if (strided) {
+    // class 0 with k-major staging, one-element copies
+    if (cplx)
+      launch_grouped<true, 32, 64, 16, 1, 4, 3, true, true, false, 0, true>(a, s);
+    else
+      launch_grouped<false, 64, 64, 32, 2, 2, 3, true, true, false, 0, true>(a, s);
+  } else if (cplx) {
     dispatch<true>(a, grid, cls, a_kmajor, b_kmajor, false, s);
-  else
+  } else {
     dispatch<false>(a, grid, cls, a_kmajor, b_kmajor, vec, s);
+  }
   NDT_CUDA(cudaEventRecord(plan->last_use, s));
 }
 

@@ -256,14 +256,34 @@ struct GroupedSegment {
   int64_t lda, ldb;
   int64_t scale_off;     // offset into the k-scale vector, or -1
 };
+// Strided operands: one GEMM index (rows, contraction or columns) of a block
+// whose axes are not in GEMM order, as at most two strided runs:
+// offset(x) = (x % e0) * s0 + (x / e0) * s1.  One run: e0 above every index.
+struct IndexRuns {
+  uint32_t e0;
+  uint32_t pad;
+  int64_t s0, s1;
+};
+struct StridedProblem {
+  IndexRuns cm, cn;  // C block: rows and columns (from c_off)
+};
+struct StridedSegment {
+  IndexRuns am, ak;  // A block: rows and contraction (from a_off)
+  IndexRuns bk, bn;  // B block: contraction and columns (from b_off)
+};
 // sm_reserve: SMs left free of the launch's persistent CTAs (room for
 // transfer kernels that run beside it, e.g. NCCL's).  peer_copies (at most
 // 7): further buffers laid out like C (other GPUs' memory mapped into this
 // process) that every output tile is also stored to as it is computed.
+// sprobs / ssegs (one per problem / segment, no k-scale): the operands and C
+// are addressed through their index runs, so permuted blocks are read and
+// written in place (lda, ldb and the majorness flags are then unused).
 void grouped_gemm(DType dt, const void* A, const void* B, void* C, bool a_kmajor, bool b_kmajor,
                   const std::vector<GroupedProblem>& probs, const std::vector<GroupedSegment>& segs,
                   const void* kscale, cudaStream_t s, bool kscale_real = false, int sm_reserve = 0,
-                  const std::vector<void*>* peer_copies = nullptr);
+                  const std::vector<void*>* peer_copies = nullptr,
+                  const std::vector<StridedProblem>* sprobs = nullptr,
+                  const std::vector<StridedSegment>* ssegs = nullptr);
 
 // Block-sparse device helpers (blocksparse_kernels.cu).  A block table entry
 // describes one block: its extents, and for the dense side its start offset

@@ -474,13 +474,67 @@ def test_from_device_blocks_sorts_and_packs(gpu, cplx):
 
 def test_cfg4_permuted_labels_many_blocks_vs_oracle(gpu, oracle):
     """U(1) rank-4 at 1/8 scale with A's labels in a non-natural order
-    (-1, 1, -2, 2): A's 489 blocks are permuted to [free, contracted] in one
-    launch before the grouped GEMM; checked against the oracle."""
+    (-1, 1, -2, 2): the grouped GEMM reads A's 489 blocks in place through
+    their index runs (rows: free axes 1, 3; contraction: axes 0, 2), so the
+    contraction is that one launch; checked against the oracle."""
     (sa, ca, a), (sb, cb, b), _, lb = cfg4_tensors(scale=8)
     # A's axes relabelled: axis 0 and 2 contracted, 1 and 3 free
     la = [-1, 1, -2, 2]
     lb2 = [-1, -2, 3, 4]
+    cls = gpu.blocksparse.BlockSparseF64
+    At, Bt = cls.from_blocks(sa, ca, a), cls.from_blocks(sb, cb, b)
+    n0 = gpu.launch_count()
+    gpu.blocksparse.contract(At, la, Bt, lb2)
+    assert gpu.launch_count() - n0 == 1
     _check(gpu, oracle, (sa, ca, a), la, (sb, cb, b), lb2)
+
+
+# Operands and output in non-GEMM axis order, each GEMM index of every block
+# in at most two strided runs: the grouped GEMM addresses the blocks in place
+# (one launch, no pack of A or B, no permute of C).
+STRIDED = [
+    # A (contracted, free, contracted, free)
+    ([[2, 3], [3, 2], [2, 4], [1, 3]], [-1, 1, -2, 2], [[2, 3], [2, 4], [4, 1], [2]], [-1, -2, 3, 4]),
+    # B (free, contracted, free, contracted), its contracted axes reversed
+    ([[3, 2], [1, 3], [2, 3], [2, 4]], [1, 2, -1, -2], [[4, 1], [2, 4], [2], [2, 3]], [3, -2, 4, -1]),
+    # both operands interleaved, contracted axes in opposite orders
+    ([[2, 2], [3, 1], [4], [2, 3]], [1, -2, 2, -1], [[2, 3], [3, 2], [3, 1], [1, 2]], [-1, 3, -2, 4]),
+    # output labels descending (every output block square): C written in its
+    # label-sorted axis order directly
+    ([[3, 3], [4, 2]], [2, -1], [[4, 2], [3, 3]], [-1, 1]),
+]
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+@pytest.mark.parametrize("sa,la,sb,lb", STRIDED)
+def test_strided_operands_one_launch_vs_oracle(gpu, oracle, sa, la, sb, lb, cplx):
+    rng = np.random.default_rng(int.from_bytes(repr((sa, la, sb, lb, cplx)).encode(), "little") % (2**32))
+    A = random_bs(rng, sa, 0.8, cplx)
+    B = random_bs(rng, sb, 0.8, cplx)
+    cls = _cls(gpu, cplx)
+    At, Bt = cls.from_blocks(*A), cls.from_blocks(*B)
+    n0 = gpu.launch_count()
+    gpu.blocksparse.contract(At, la, Bt, lb)
+    assert gpu.launch_count() - n0 == 1
+    _check(gpu, oracle, A, la, B, lb)
+
+
+@pytest.mark.parametrize("cplx", [False, True])
+def test_three_runs_fall_back_to_packing(gpu, oracle, cplx):
+    """A's free axes 1, 3, 5 lie in three separate runs: its blocks are
+    packed first (more than one launch), with the same result."""
+    rng = np.random.default_rng(606 + cplx)
+    sa = [[2, 1], [1, 2], [2, 2], [3, 1], [1, 2], [2, 1]]
+    sb = [[2, 1], [2, 2], [1, 2], [2, 3]]
+    A = random_bs(rng, sa, 0.9, cplx)
+    B = random_bs(rng, sb, 0.9, cplx)
+    la, lb = [-1, 1, -2, 2, -3, 3], [-1, -2, -3, 4]
+    cls = _cls(gpu, cplx)
+    At, Bt = cls.from_blocks(*A), cls.from_blocks(*B)
+    n0 = gpu.launch_count()
+    gpu.blocksparse.contract(At, la, Bt, lb)
+    assert gpu.launch_count() - n0 >= 2
+    _check(gpu, oracle, A, la, B, lb)
 
 
 def test_cfg4_permutedims_many_blocks_bit_exact(gpu, oracle):
