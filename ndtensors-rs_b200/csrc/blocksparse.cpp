@@ -547,11 +547,16 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
     // index of every block takes at most two runs and every block has fewer
     // than 2^31 elements (no k-scale), and when that is not slower: complex
     // tiles lose nothing measurable to the one-element copies (B200, the c128
-    // MPS chain with A's axes permuted: 31.4 TFLOP/s either way), f64 tiles
-    // about 8% (U(1) rank-4 half scale with A's labels (-1, 1, -2, 2): 27.6
-    // TFLOP/s against 29.6 with A packed first), so f64 takes the strided
-    // path while 8% of its GEMM time (at 30 TFLOP/s) stays below the passes
-    // it saves (each a read and a write at 6 TB/s, plus 5 us).
+    // MPS chain with A's axes permuted: 31.4 TFLOP/s either way); f64 tiles
+    // copy adjacent k pairs when every contraction run has stride 1 and an
+    // even first extent and every row offset is even (the grouped kernel's
+    // check; U(1) rank-4 half scale with A's labels (-1, 1, -2, 2): 30.8
+    // TFLOP/s in place against 29.6 with A packed first), and otherwise lose
+    // about 8% to one-element copies (U(1) rank-4
+    // half scale with A's labels (-1, 1, -2, 2): 27.6 TFLOP/s against 29.6
+    // with A packed first), so then they take the strided path only while 8%
+    // of their GEMM time (at 30 TFLOP/s) stays below the passes it saves
+    // (each a read and a write at 6 TB/s, plus 5 us).
     const bool permute_out = P->permute_c;  // the stored C layout, for the runs
     auto seg_runs = [&](size_t a, size_t b, StridedSegment* ss) -> bool {
       std::vector<int64_t> ea(na), eb(nb);
@@ -582,14 +587,21 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
       return index_runs(mi, ext, str, &sp->cm) && index_runs(ni, ext, str, &sp->cn);
     };
     if ((P->pack_a || P->pack_b || P->permute_c) && td_pos == SIZE_MAX) {
-      bool ok = true;
+      bool ok = true, pairs = true;
       double flops = 0;
+      auto even = [](int64_t x) { return x % 2 == 0; };
+      auto pair_ok = [&](const IndexRuns& rows, const IndexRuns& k, int64_t off) {
+        return k.s0 == 1 && (k.e0 == 0x7fffffffu || k.e0 % 2 == 0) && even(k.s1) && even(rows.s0) &&
+               even(rows.s1) && even(off);
+      };
       for (size_t ob = 0; ok && ob < C.nnzb(); ob++) {
         StridedProblem sp{};
         ok = prob_runs(ob, &sp);
         for (auto& p2 : contrib[C.coords[ob]]) {
           StridedSegment ss{};
           if (!ok || !(ok = seg_runs(p2.first, p2.second, &ss))) break;
+          pairs = pairs && pair_ok(ss.am, ss.ak, (int64_t)A.offs[p2.first]) &&
+                  pair_ok(ss.bn, ss.bk, (int64_t)B.offs[p2.second]);
           double m = 1, n = 1, k = 1;
           for (size_t i : ua) m *= (double)A.bsz[i][A.coords[p2.first][i]];
           for (size_t j : ub) n *= (double)B.bsz[j][B.coords[p2.second][j]];
@@ -597,7 +609,7 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
           flops += 2 * m * n * k;
         }
       }
-      if (ok && A.dt != DType::C128) {
+      if (ok && A.dt != DType::C128 && !pairs) {
         const double es = (double)esize(A.dt);
         double saved = 0;
         if (P->pack_a) saved += 2 * (double)A.total() * es / 6e12 + 5e-6;

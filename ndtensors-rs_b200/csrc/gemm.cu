@@ -517,16 +517,18 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1) dmma_gemm_kernel(c
 // interior tiles take an unpredicated path.
 // A tile whose block has no contracted extent (all its segments empty) runs
 // one k-step of zeros and writes a zero tile.
-// STR (with AK, BKM, one-element copies and no k-scale): A, B and C are
-// addressed through each segment's and problem's index runs, so blocks whose
-// axes are not in GEMM order are read and written in place.  A thread's copy
-// rows keep one offset each per segment (set when the segment starts); its
-// contraction column adds one offset per stage.
+// STR (with AK, BKM and no k-scale): A, B and C are addressed through each
+// segment's and problem's index runs, so blocks whose axes are not in GEMM
+// order are read and written in place.  A thread's copy rows keep one offset
+// each per segment (set when the segment starts); its contraction column
+// adds one offset per stage.  With VEC (f64) a copy is a pair of adjacent k
+// values: every segment's contraction runs have stride 1 and an even first
+// extent, and every offset of a pair's first value is even.
 template <bool CPLX, int BM, int BN, int BK, int WM_WARPS, int WN_WARPS, int STAGES, bool AK, bool BKM, bool VEC,
           int SCALE, bool STR = false>
 __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     dmma_grouped_kernel(const __grid_constant__ KArgs args) {
-  static_assert(!STR || (AK && BKM && !VEC && SCALE == 0), "strided operands: k-major staging, no k-scale");
+  static_assert(!STR || (AK && BKM && SCALE == 0), "strided operands: k-major staging, no k-scale");
   pdl_release();
   pdl_wait();  // before the first global access (tile tables, operands)
   using C = Cfg<CPLX, BM, BN, BK, WM_WARPS, WN_WARPS, STAGES, AK, BKM, SCALE>;
@@ -637,31 +639,36 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     const int64_t krem = kseg - k0;  // k rows left in this segment
     if (tid == 0) s_kvalid[stage] = krem < BK ? (int)krem : BK;
     if constexpr (STR) {
-      // A rows m (a_row), column k0 + a_c; B rows n (b_row), column k0 + b_c
-      const bool aok = a_c < krem, bok = b_c < krem;
-      const int64_t ka = aok ? a_off + run_off(r_ak, (uint32_t)(k0 + a_c)) : 0;
-      const int64_t kb = bok ? b_off + run_off(r_bk, (uint32_t)(k0 + b_c)) : 0;
+      // A rows m (a_row), column(s) k0 + a_c (+1); B rows n (b_row), k0 + b_c (+1)
+      const int64_t ar = krem - a_c, br = krem - b_c;
+      const int an = ar >= PW ? PW : (ar > 0 ? (int)ar : 0), bn = br >= PW ? PW : (br > 0 ? (int)br : 0);
+      const int64_t ka = an ? a_off + run_off(r_ak, (uint32_t)(k0 + a_c)) : 0;
+      const int64_t kb = bn ? b_off + run_off(r_bk, (uint32_t)(k0 + b_c)) : 0;
       double* da = As + ((size_t)a_r * LDA + a_c) * RPL;
       double* db = Bs + ((size_t)b_r * LDB + b_c) * RPL;
 #pragma unroll
       for (int it = 0; it < PlanA::IT; it++) {
-        const bool ok = aok && it * PlanA::RS < a_mrem - a_r;
-        const char* p = ok ? Ab + (ka + a_row[it]) * ES : Ab;
+        const int nb = it * PlanA::RS < a_mrem - a_r ? an : 0;
+        const char* p = nb ? Ab + (ka + a_row[it]) * ES : Ab;
         double* d = da + (size_t)it * PlanA::RS * LDA * RPL;
         if constexpr (CPLX)
-          cp_async16n(d, p, ok ? 16 : 0);
+          cp_async16n(d, p, nb * 16);
+        else if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
         else
-          cp_async8(d, p, ok);
+          cp_async8(d, p, nb != 0);
       }
 #pragma unroll
       for (int it = 0; it < PlanB::IT; it++) {
-        const bool ok = bok && it * PlanB::RS < b_nrem - b_r;
-        const char* p = ok ? Bb + (kb + b_row[it]) * ES : Bb;
+        const int nb = it * PlanB::RS < b_nrem - b_r ? bn : 0;
+        const char* p = nb ? Bb + (kb + b_row[it]) * ES : Bb;
         double* d = db + (size_t)it * PlanB::RS * LDB * RPL;
         if constexpr (CPLX)
-          cp_async16n(d, p, ok ? 16 : 0);
+          cp_async16n(d, p, nb * 16);
+        else if constexpr (PW == 2)
+          cp_async16n(d, p, nb * 8);
         else
-          cp_async8(d, p, ok);
+          cp_async8(d, p, nb != 0);
       }
       return;
     }
@@ -1433,9 +1440,21 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   for (const GroupedSegment& sg : segs)
     vec = vec && sg.a_off % 2 == 0 && sg.b_off % 2 == 0 && sg.lda % 2 == 0 && sg.ldb % 2 == 0;
   if (strided) {
-    // class 0 with k-major staging, one-element copies
+    // class 0 with k-major staging; f64 pair copies when every pair is
+    // adjacent (contraction runs of stride 1, even first extent) and 16-byte
+    // aligned (even offsets)
+    auto even = [](int64_t x) { return x % 2 == 0; };
+    auto pairs = [&](const IndexRuns& rows, const IndexRuns& k, int64_t off) {
+      return k.s0 == 1 && (k.e0 == 0x7fffffffu || k.e0 % 2 == 0) && even(k.s1) && even(rows.s0) && even(rows.s1) &&
+             even(off);
+    };
+    bool pv = aligned16(A) && aligned16(B);
+    for (size_t q = 0; pv && q < segs.size(); q++)
+      pv = pairs((*ssegs)[q].am, (*ssegs)[q].ak, segs[q].a_off) && pairs((*ssegs)[q].bn, (*ssegs)[q].bk, segs[q].b_off);
     if (cplx)
       launch_grouped<true, 32, 64, 16, 1, 4, 3, true, true, false, 0, true>(a, s);
+    else if (pv)
+      launch_grouped<false, 64, 64, 32, 2, 2, 3, true, true, true, 0, true>(a, s);
     else
       launch_grouped<false, 64, 64, 32, 2, 2, 3, true, true, false, 0, true>(a, s);
   } else if (cplx) {

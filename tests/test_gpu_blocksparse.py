@@ -519,6 +519,38 @@ def test_strided_operands_one_launch_vs_oracle(gpu, oracle, sa, la, sb, lb, cplx
     _check(gpu, oracle, A, la, B, lb)
 
 
+def test_strided_pairs_vs_oracle(gpu, oracle):
+    """Even block extents and A's contraction run contiguous: the strided
+    f64 loads copy adjacent k pairs (16 bytes); one launch, vs the oracle."""
+    rng = np.random.default_rng(2024)
+    sa, la = [[2, 4], [4, 2], [2, 6], [2, 4]], [-1, 1, -2, 2]
+    sb, lb = [[2, 4], [2, 6], [4, 2], [2]], [-1, -2, 3, 4]
+    A = random_bs(rng, sa, 0.8, False)
+    B = random_bs(rng, sb, 0.8, False)
+    cls = _cls(gpu, False)
+    At, Bt = cls.from_blocks(*A), cls.from_blocks(*B)
+    n0 = gpu.launch_count()
+    gpu.blocksparse.contract(At, la, Bt, lb)
+    assert gpu.launch_count() - n0 == 1
+    _check(gpu, oracle, A, la, B, lb)
+
+
+def test_cfg4_quarter_scale_permuted_equals_natural(gpu):
+    """U(1) rank-4 at 1/4 scale (even sector dims: pair copies): A's blocks
+    permuted to (-1, 1, -2, 2) and contracted in place give the same bits as
+    the natural-order contraction, in one launch."""
+    (sa, ca, a), (sb, cb, b), la, lb = cfg4_tensors(scale=4)
+    cls = gpu.blocksparse.BlockSparseF64
+    At, Bt = cls.from_blocks(sa, ca, a), cls.from_blocks(sb, cb, b)
+    ref = gpu.blocksparse.contract(At, la, Bt, lb)
+    Ap = At.permutedims([2, 0, 3, 1])
+    n0 = gpu.launch_count()
+    got = gpu.blocksparse.contract(Ap, [-1, 1, -2, 2], Bt, [-1, -2, 3, 4])
+    assert gpu.launch_count() - n0 == 1
+    assert got.coords == ref.coords and got.block_sizes == ref.block_sizes
+    assert np.array_equal(got.to_numpy_data(), ref.to_numpy_data())
+
+
 @pytest.mark.parametrize("cplx", [False, True])
 def test_three_runs_fall_back_to_packing(gpu, oracle, cplx):
     """A's free axes 1, 3, 5 lie in three separate runs: its blocks are
