@@ -384,10 +384,13 @@ void ndt_b200_comm_release(ndt_comm* comm);
 /* contract_blocksparse with the output gathered on every rank (the contract
  * "gather" flag; device list = the communicator's ranks).  Every rank passes
  * the same operands; each computes its share of the output blocks (longest
- * processing time on tile cost, as contract_shard) into its slot of a staging
- * buffer, chunk by chunk; an NCCL all-gather per chunk runs while the next
- * chunk computes, and one copy kernel puts every block at its place in the
- * packed, sorted output.  Every rank returns
+ * processing time on tile cost, as contract_shard).  On up to 8 ranks that
+ * map each other's memory (CUDA IPC), the GEMM stores every output tile into
+ * every rank's output buffer as it computes it, a barrier follows, and each
+ * rank copies its buffer into the result; otherwise each rank computes into
+ * its slot of a staging buffer, an NCCL all-gather follows, and one copy
+ * kernel puts every block at its place in the packed, sorted output.  Every
+ * rank returns
  * the unsharded result (same structure and values as
  * ndt_blocksparse_*_contract).  Collective: every rank of the communicator
  * must call it, with the same arguments. */

@@ -741,11 +741,13 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
 // gathered contraction).  With nranks > 1 only this rank's output blocks are
 // computed and stored (longest processing time on the tile cost; every rank
 // derives the same assignment).  `gcomm` (gathered mode): rank and nranks are
-// the communicator's; this rank computes its share of the output blocks into
-// its slot of a staging buffer, chunk by chunk, an NCCL all-gather per chunk
-// runs behind the next chunk's compute, and one copy kernel puts every block
-// at its place in the sorted output.  The result is the unsharded tensor on
-// every rank.
+// the communicator's; when the ranks map each other's output buffers, the
+// grouped launch stores every tile of this rank's output blocks into all of
+// them as it computes it, then a barrier and a copy into the result;
+// otherwise this rank computes into its slot of a staging buffer, chunk by
+// chunk, an NCCL all-gather per chunk follows, and one copy kernel puts every
+// block at its place in the sorted output.  The result is the unsharded
+// tensor on every rank.
 BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, const BlockSparseT& B,
                          const std::vector<int32_t>& lb, int rank, int nranks, ShardPlan* plan_only = nullptr,
                          const size_t* select = nullptr, size_t nsel = 0, const ThroughDiag* td = nullptr,

@@ -465,9 +465,10 @@ class Comm:
 def contract_gathered(a, labels_a, b, labels_b, comm: Comm):
     """contract() with the work split over the communicator's ranks and the
     result gathered on every rank (collective: every rank calls it with the
-    same operands).  Each rank computes its share of the output blocks into
-    their places in the output and receives the others' over NCCL while it
-    computes."""
+    same operands).  Each rank computes its share of the output blocks and
+    stores every tile into every rank's output buffer as it computes it (the
+    ranks map each other's buffers); when they cannot, each rank's blocks are
+    gathered with an NCCL all-gather."""
     la, na = _labels(labels_a)
     lb, nb = _labels(labels_b)
     st = ctypes.c_int(-999)
