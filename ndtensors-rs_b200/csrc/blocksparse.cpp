@@ -283,6 +283,9 @@ struct ContractPlan {
   // gathered mode, ranks mapping each other's memory: this rank's blocks at
   // their places in the sorted output, computed once and stored to every rank
   PlannedLaunch direct;
+  // ... and the other ranks' blocks (byte ranges, adjacent blocks merged),
+  // copied from the mapped buffer into the result once they have arrived
+  std::vector<int64_t> peer_off, peer_bytes;
 };
 
 namespace {
@@ -713,6 +716,16 @@ std::shared_ptr<const ContractPlan> plan_contract(const BlockSparseT& A, const s
         for (size_t i = 0; i < all_out.size(); i++)
           if (owner[i] == rank) mine.push_back(i);
         make_table(mine, P->direct);
+        for (size_t i = 0; i < all_out.size(); i++) {
+          const int64_t o = (int64_t)(C.offs[i] * es), n = (int64_t)((C.offs[i + 1] - C.offs[i]) * es);
+          if (owner[i] == rank || n == 0) continue;
+          if (!P->peer_off.empty() && P->peer_off.back() + P->peer_bytes.back() == o)
+            P->peer_bytes.back() += n;
+          else {
+            P->peer_off.push_back(o);
+            P->peer_bytes.push_back(n);
+          }
+        }
       }
       for (size_t i = 0; i < all_out.size(); i++) {
         const size_t n = C.offs[i + 1] - C.offs[i];
@@ -801,17 +814,18 @@ BlockSparseT bs_contract(const BlockSparseT& A, const std::vector<int32_t>& la, 
   const bool direct = gcomm && nranks > 1 && comm_symmetric(*gcomm, C.total() * es, s, &mine, peers.data());
   if (direct) {
     // One launch computes this rank's output blocks and stores every tile
-    // into this rank's mapped buffer and into every other rank's, over
+    // into the result and into every other rank's mapped buffer, over
     // NVLink, as it is computed (no separate transfer); a barrier over the
-    // ranks, then the buffer is copied into the result.
+    // ranks, then the other ranks' blocks are copied from this rank's mapped
+    // buffer into the result.
     std::vector<void*> others;
     for (int r = 0; r < nranks; r++)
       if (r != rank) others.push_back(peers[r]);
     if (!P->direct.probs.empty())
-      grouped_gemm(A.dt, Ad, Bd, mine, P->a_kmajor, P->b_kmajor, P->direct.probs, P->direct.segs, kscale, s, kreal,
+      grouped_gemm(A.dt, Ad, Bd, Cu, P->a_kmajor, P->b_kmajor, P->direct.probs, P->direct.segs, kscale, s, kreal,
                    0, &others, sruns(P->direct), sruns_seg(P->direct));
     comm_barrier(*gcomm, s, s);
-    NDT_CUDA(cudaMemcpyAsync(Cu, mine, C.total() * es, cudaMemcpyDeviceToDevice, s));
+    copy_segments(mine, Cu, P->peer_off, P->peer_off, P->peer_bytes, s);
   } else if (gcomm) {
     // Staged: each chunk into this rank's slots of a staging buffer, an
     // in-place NCCL all-gather per chunk, one copy into the sorted output.
