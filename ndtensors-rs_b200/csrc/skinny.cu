@@ -18,8 +18,10 @@
 //     In the DMRG steps the fastest axis of i is the fastest of X, so a
 //     warp's copies of one l are 256 contiguous bytes;
 //   * the arithmetic runs on the FP64 tensor cores (mma.sync m16n8k8 f64):
-//     k is padded to KS * 8 (the padding rows of every stage are zeroed once)
-//     and n to NT * 8; Y's fragments stay in registers for the whole kernel.
+//     k is padded to KS * 8 (the padding rows of every stage are zeroed once;
+//     a last step holding at most 4 values is one m16n8k4 MMA, so k = 10
+//     costs 1.5 steps of tensor work, not 2) and n to NT * 8; Y's fragments
+//     stay in registers for the whole kernel.
 //     Each warp owns 32 rows of a tile (two m16 fragments), so 32 rows cost
 //     2 * KS * NT tensor instructions and 8 * KS fragment loads; complex
 //     values take four real products (re*re - im*im, re*im + im*re);
@@ -112,6 +114,14 @@ __device__ __forceinline__ void dmma(double (&c)[4], const double (&a)[4], const
       : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
       : "d"(a[0]), "d"(a[1]), "d"(a[2]), "d"(a[3]), "d"(b[0]), "d"(b[1]));
 }
+// k = 4 step: A values (row g, col t), (row g + 8, col t) -- the first two of
+// the k = 8 fragment -- and B (row t, col g), its first value.
+__device__ __forceinline__ void dmma_k4(double (&c)[4], const double (&a)[4], const double (&b)[2]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+d"(c[0]), "+d"(c[1]), "+d"(c[2]), "+d"(c[3])
+      : "d"(a[0]), "d"(a[1]), "d"(b[0]));
+}
 
 template <bool CPLX>
 struct Elem;
@@ -148,6 +158,9 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
   const T* Y = static_cast<const T*>(a.Y);
   T* C = static_cast<T*>(a.C);
   const int64_t cjt = 2 * t * a.cj;  // this lane's first output column
+  // k not a multiple of 8 with at most 4 values in its last k = 8 step: that
+  // step is one k = 4 MMA (a quarter of the tensor work at k = 10)
+  const bool tail4 = (a.k & 7) != 0 && (a.k & 7) <= 4;
   // per-lane constants: fragment row offsets (rows l >= k read the zero row)
   int foff[KS][2];
 #pragma unroll
@@ -310,9 +323,15 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
         for (int q = 0; q < 4; q++) cr[nt][q] = ci[nt][q] = 0.0;
 #pragma unroll
       for (int ks = 0; ks < KS; ks++) {
+        // the last step holds at most 4 contracted values: one k = 4 MMA
+        const bool k4 = ks == KS - 1 && tail4;
         double ar[4], ai[4], nai[4];
 #pragma unroll
         for (int q = 0; q < 4; q++) {
+          if (k4 && q >= 2) {
+            ar[q] = ai[q] = nai[q] = 0.0;
+            continue;
+          }
           const T v = xs[foff[ks][q >> 1] + row0 + 8 * (q & 1)];
           if constexpr (CPLX) {
             ar[q] = v.x;
@@ -322,13 +341,25 @@ __global__ void __launch_bounds__(kThreads, (!CPLX && KS <= 2 && NT <= 2) ? 3 : 
             ar[q] = v;
           }
         }
+        if (k4) {
 #pragma unroll
-        for (int nt = 0; nt < NT; nt++) {
-          dmma(cr[nt], ar, br[ks][nt]);
-          if constexpr (CPLX) {
-            dmma(cr[nt], nai, bi[ks][nt]);
-            dmma(ci[nt], ar, bi[ks][nt]);
-            dmma(ci[nt], ai, br[ks][nt]);
+          for (int nt = 0; nt < NT; nt++) {
+            dmma_k4(cr[nt], ar, br[ks][nt]);
+            if constexpr (CPLX) {
+              dmma_k4(cr[nt], nai, bi[ks][nt]);
+              dmma_k4(ci[nt], ar, bi[ks][nt]);
+              dmma_k4(ci[nt], ai, br[ks][nt]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int nt = 0; nt < NT; nt++) {
+            dmma(cr[nt], ar, br[ks][nt]);
+            if constexpr (CPLX) {
+              dmma(cr[nt], nai, bi[ks][nt]);
+              dmma(ci[nt], ar, bi[ks][nt]);
+              dmma(ci[nt], ai, br[ks][nt]);
+            }
           }
         }
       }
