@@ -144,10 +144,11 @@ struct Cfg {
   // SCALE: each stage also holds the BK scale values of its k range
   static constexpr int stage_elems = PA::elems + PB::elems + (SCALE ? BK : 0);
   static constexpr size_t smem_bytes = (size_t)STAGES * stage_elems * ES;
-  // complex grouped launches with peer copies of C: per warp, 8 columns of
-  // its tile (pitch WM + 1 elements) staged for the bulk copies to the peers
-  static constexpr int push_pitch = WM + 1;
-  static constexpr size_t push_bytes = CPLX ? (size_t)(kThreads / 32) * 8 * push_pitch * ES : 0;
+  // complex grouped launches with peer copies of C: per column group (the
+  // WM_WARPS warps holding the same columns), 8 columns of the CTA tile
+  // (pitch BM + 1 elements) staged for the bulk copies to the peers
+  static constexpr int push_pitch = BM + 1;
+  static constexpr size_t push_bytes = CPLX ? (size_t)WN_WARPS * 8 * push_pitch * ES : 0;
 };
 
 // Copy pattern of one operand tile: ROWS x CONT elements in shared memory
@@ -761,24 +762,43 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
     }
     if constexpr (CPLX && !STR) {
       if (np > 0) {
-        // Each 8-column group of the warp tile is stored into C and staged in
-        // shared memory; bulk copies then send each staged column (the warp's
-        // rows of it, contiguous in C) to every peer copy.  The warp goes on
-        // to the next tile while the copies drain; it waits only before it
-        // overwrites the staging, until the copies have read it.
+        // The WM_WARPS warps holding the same columns of the CTA tile store
+        // them into C and stage 8 of them at a time, all BM rows; bulk copies
+        // then send each staged column (the tile's rows of it, contiguous in
+        // C: up to BM * 16 bytes per copy) to every peer copy.  The warps go
+        // on to the next tile while the copies drain; they wait only before
+        // they overwrite the staging, until the copies have read it.  Every
+        // warp of a group passes the same group barriers (the epilogue runs
+        // on all warps of the CTA together).
+        const int grp = warp / WM_WARPS;
         double2* stg = reinterpret_cast<double2*>(smem + C::smem_bytes / sizeof(double)) +
-                       (size_t)warp * 8 * C::push_pitch;
-        const int64_t r0 = cm0 + wm0;
+                       (size_t)grp * 8 * C::push_pitch;
+        const int nrows = cm - cm0 < BM ? (int)(cm - cm0) : BM;  // rows of the CTA tile in the block
+        auto group_sync = [&]() {
+          __syncwarp();
+          if constexpr (WM_WARPS > 1) {
+            static_assert(WN_WARPS <= 4, "one named barrier (1..4) per column group");
+            constexpr int n = WM_WARPS * 32;
+            if (grp == 0)
+              asm volatile("bar.sync 1, %0;\n" ::"n"(n) : "memory");
+            else if (grp == 1)
+              asm volatile("bar.sync 2, %0;\n" ::"n"(n) : "memory");
+            else if (grp == 2)
+              asm volatile("bar.sync 3, %0;\n" ::"n"(n) : "memory");
+            else
+              asm volatile("bar.sync 4, %0;\n" ::"n"(n) : "memory");
+          }
+        };
 #pragma unroll
         for (int j = 0; j < NT; j++) {
           bulk_wait_read();
-          __syncwarp();
+          group_sync();
 #pragma unroll
           for (int i = 0; i < MT; i++)
 #pragma unroll
             for (int q = 0; q < 4; q++) {
-              const int rl = i * 16 + g + 8 * (q >> 1), cl = 2 * t + (q & 1);
-              const int64_t row = r0 + rl, col = cn0 + wn0 + j * 8 + cl;
+              const int rl = wm0 + i * 16 + g + 8 * (q >> 1), cl = 2 * t + (q & 1);
+              const int64_t row = cm0 + rl, col = cn0 + wn0 + j * 8 + cl;
               const double x = acc[i][j][q], y = acc[i][j][4 + q], z = acc[i][j][8 + q];
               double2 v = make_double2(x - y, z - x - y);
               if (row < cm && col < cn) {
@@ -795,15 +815,14 @@ __global__ void __launch_bounds__(WM_WARPS* WN_WARPS * 32, 1)
               for (int pl = 0; pl < PLANES; pl++) acc[i][j][4 * pl + q] = 0.0;
             }
           fence_shared_to_bulk();
-          __syncwarp();
-          if (mrows > 0)
-            for (int e = lane; e < 8 * np; e += 32) {
-              const int cl = e & 7;
-              const int64_t col = cn0 + wn0 + j * 8 + cl;
-              if (col < cn)
-                bulk_store(args.peer_c[e >> 3] + (c_off + r0 + col * cm) * ES, stg + cl * C::push_pitch,
-                           (unsigned)mrows * ES);
-            }
+          group_sync();
+          for (int e = (warp % WM_WARPS) * 32 + lane; e < 8 * np; e += 32 * WM_WARPS) {
+            const int cl = e & 7;
+            const int64_t col = cn0 + wn0 + j * 8 + cl;
+            if (col < cn)
+              bulk_store(args.peer_c[e >> 3] + (c_off + cm0 + col * cm) * ES, stg + cl * C::push_pitch,
+                         (unsigned)nrows * ES);
+          }
           bulk_commit();
         }
         return;
@@ -1358,7 +1377,10 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
   // block structure), which then cost one launch and no host planning.
   PlanKey key;
   key.device = c.device;
-  key.flags = (cplx ? 1 : 0) | (strided ? 2 : 0);
+  // complex launches that push their tiles to peer copies take class 1:
+  // its 64-row tiles send 1 KB per column and peer instead of 512 bytes
+  const bool push64 = cplx && !strided && peer_copies && !peer_copies->empty();
+  key.flags = (cplx ? 1 : 0) | (strided ? 2 : 0) | (push64 ? 4 : 0);
   const size_t bp = probs.size() * sizeof(GroupedProblem), bsg = segs.size() * sizeof(GroupedSegment);
   const size_t bsp = strided ? sprobs->size() * sizeof(StridedProblem) : 0;
   const size_t bss = strided ? ssegs->size() * sizeof(StridedSegment) : 0;
@@ -1378,7 +1400,8 @@ void grouped_gemm(DType dt, const void* A, const void* B, void* Cp, bool a_kmajo
     std::vector<int4> tiles, cand;
     int cls = 0;
     double best = -1;
-    for (int cl = 0; cl < (strided ? 1 : nclasses(cplx)); cl++) {  // strided: class 0 only
+    const int cl0 = push64 ? 1 : 0, cl1 = strided ? 1 : (push64 ? 2 : nclasses(cplx));  // strided: class 0 only
+    for (int cl = cl0; cl < cl1; cl++) {
       double t;
       build(cl, cand, &t);
       if (best < 0 || t < best) {
