@@ -419,8 +419,9 @@ ndt_blocksparse_c64* ndt_blocksparse_c64_allgather(const ndt_blocksparse_c64* sh
 
 /* Dense f64 contraction that allocates no memory (no counterpart in the
  * reference).  For callers that may not call cudaMalloc -- allocation-free
- * hot loops, hosts that own the device memory budget, graph-oriented
- * runtimes.  Same label semantics as ndt_tensor_f64_contract; inputs and the
+ * hot loops, hosts that own the device memory budget, runtimes that forbid
+ * allocation on their hot path.  Same label semantics as
+ * ndt_tensor_f64_contract; inputs and the
  * output are caller-owned device buffers (column-major, A and B dense over
  * their shapes, zero extents rejected with NDT_INTERNAL_ERROR); c must hold
  * c_len >= output length elements; out_shape (may be NULL) receives the

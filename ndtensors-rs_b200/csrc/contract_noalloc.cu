@@ -1,9 +1,9 @@
 // Dense f64 contraction that allocates nothing.
 //
-// Some callers cannot call cudaMalloc: code running inside a CUDA-graph-
-// oriented runtime that forbids allocation on its hot path, plugins hosted by
-// an application that owns the device memory budget, or real-time loops
-// where an allocation (and its implicit synchronisation) is not allowed.  For
+// Some callers cannot call cudaMalloc: code running inside a runtime that
+// forbids allocation on its hot path, plugins hosted by an application that
+// owns the device memory budget, or real-time loops where an allocation (and
+// its implicit synchronisation) is not allowed.  For
 // them this file provides ndt_b200_contract_f64_noalloc: the same contraction
 // as ndt_tensor_f64_contract (the reference's naive-loop label semantics:
 // output axes are A's positive labels then B's, unmatched negative labels are
